@@ -1,0 +1,19 @@
+"""forgetune_b200: a B200 (sm_100a) backend for ForgeTune's compiled forward pass.
+
+``compile_model`` lowers a torch model, fuses and plans it in the native
+engine, and returns a :class:`CompiledModel` whose per-model shared library
+exports the reference's C ABI and runs on hand-written CUDA kernels.
+"""
+
+from .compiler import CompiledModel, compile_model
+from .errors import (AutotuningError, CodeGenError, CompilationError, CorrectnessError, ForgeTuneError,
+                     ForgeTuneRuntimeError, InvalidGraphError, InvalidShapeError, UnsupportedOpError)
+from .frontend import IRGraph, export_to_ir
+from .runtime import NativeRuntime
+
+__version__ = "0.1.0"
+__all__ = [
+    "compile_model", "CompiledModel", "NativeRuntime", "IRGraph", "export_to_ir",
+    "ForgeTuneError", "UnsupportedOpError", "InvalidGraphError", "InvalidShapeError", "CodeGenError",
+    "CompilationError", "CorrectnessError", "AutotuningError", "ForgeTuneRuntimeError",
+]

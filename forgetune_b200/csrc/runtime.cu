@@ -1,0 +1,1087 @@
+// CUDA runtime behind the C ABI: device weight replicas, per-thread execution
+// contexts (one cudaMalloc'd block holding the planned arena and the staging
+// buffers), CUDA-graph replay of the launch list, the host<->device copy
+// pipeline and the kernel dispatch.
+//
+// Lifetime mirrors the reference's generated runtime (src/codegen.cpp:113-275):
+// a context is leased per call from a pool owned by the calling thread, a
+// nested call on the same thread leases another one, and after the first call
+// on a thread no further allocation happens.  The allocation counters report
+// the same events the reference counts (payload allocations and pool
+// insertions, per thread; a process-wide total).
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <atomic>
+#include <chrono>
+#include <cstdio>
+#include <cstring>
+#include <memory>
+#include <mutex>
+#include <stdexcept>
+#include <thread>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "elementwise.cuh"
+#include "engine.hpp"
+#include "philox.cuh"
+#include "simt_gemm.cuh"
+#include "tc_gemm.cuh"
+
+#define FTB_API extern "C" __attribute__((visibility("default")))
+
+namespace ftb {
+
+// ---------------------------------------------------------------------------
+// status codes (include/forgetune_b200.h)
+// ---------------------------------------------------------------------------
+enum Status : int {
+  ST_OK = 0,
+  ST_NULL = -1,
+  ST_INPUT = -2,
+  ST_OUTPUT = -3,
+  ST_ALLOC = -4,
+  ST_DEVICE = -5,
+  ST_CONFIG = -6,
+};
+
+static thread_local std::string t_last_error;
+
+static void set_error(const std::string& s) { t_last_error = s; }
+
+#define CUDA_TRY(expr)                                                                 \
+  do {                                                                                 \
+    cudaError_t _e = (expr);                                                           \
+    if (_e != cudaSuccess) {                                                           \
+      set_error(std::string(#expr) + ": " + cudaGetErrorString(_e));                  \
+      return ST_DEVICE;                                                                \
+    }                                                                                  \
+  } while (0)
+
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev) {
+    if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+    if (prev != dev) cudaSetDevice(dev);
+  }
+  ~DeviceGuard() {
+    int cur = -1;
+    if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+// ---------------------------------------------------------------------------
+// device replica of the weights + launch list
+// ---------------------------------------------------------------------------
+struct Replica {
+  int device = -1;
+  float* weights = nullptr;  // blob weights followed by derived layouts
+  size_t weight_floats = 0;
+  std::vector<Step> steps;
+  std::vector<ConvGeom> conv;  // per step (valid for ST_CONV)
+  std::vector<TcWeights> tc;   // per step (valid when the tensor-core path may run)
+  int sm_count = 148;
+};
+
+struct ExecCtx {
+  int device = -1;
+  cudaStream_t stream = nullptr;   // compute
+  cudaStream_t h2d = nullptr;      // host -> device copies
+  cudaStream_t d2h = nullptr;      // device -> host copies
+  char* block = nullptr;           // the one allocation: arena | input | output
+  size_t block_bytes = 0;
+  char* arena = nullptr;
+  float* d_in = nullptr;
+  float* d_out = nullptr;
+  std::vector<cudaEvent_t> ev_in, ev_out;  // per pipeline chunk
+  cudaEvent_t ev_a = nullptr, ev_b = nullptr;
+  std::vector<cudaEvent_t> prof;  // [slot][step + 1] step-boundary events
+  bool in_use = false;
+  struct CachedGraph {
+    int64_t batch;
+    const float* in;
+    float* out;
+    cudaGraphExec_t exec;
+  };
+  std::vector<CachedGraph> graphs;
+};
+
+struct ThreadPool {
+  std::vector<ExecCtx*> ctxs;
+  size_t payload_allocs = 0;
+  size_t block_insertions = 0;
+};
+
+struct Model;
+
+// Registry of live models; leaked on purpose so thread-exit destructors that
+// run during process teardown can still consult it safely.
+struct Registry {
+  std::mutex mu;
+  std::unordered_map<uint64_t, Model*> live;
+  std::atomic<uint64_t> next_uid{1};
+};
+static Registry* registry() {
+  static Registry* r = new Registry;
+  return r;
+}
+
+struct Model {
+  uint64_t uid = 0;
+  Program prog;
+  std::vector<int> devices;  // empty: the caller's current device at first use
+  std::vector<std::unique_ptr<Replica>> replicas;
+  std::vector<ExecCtx*> all_ctxs;
+  std::mutex mu;
+  std::atomic<size_t> process_allocs{0};
+  bool allow_tc = true;
+};
+
+static void destroy_ctx(ExecCtx* c) {
+  if (!c) return;
+  DeviceGuard g(c->device);
+  for (auto& cg : c->graphs) cudaGraphExecDestroy(cg.exec);
+  for (auto e : c->ev_in) cudaEventDestroy(e);
+  for (auto e : c->ev_out) cudaEventDestroy(e);
+  for (auto e : c->prof) cudaEventDestroy(e);
+  if (c->ev_a) cudaEventDestroy(c->ev_a);
+  if (c->ev_b) cudaEventDestroy(c->ev_b);
+  if (c->stream) cudaStreamDestroy(c->stream);
+  if (c->h2d) cudaStreamDestroy(c->h2d);
+  if (c->d2h) cudaStreamDestroy(c->d2h);
+  if (c->block) cudaFree(c->block);
+  delete c;
+}
+
+// thread-local pools keyed by (model uid, device)
+struct PoolKey {
+  uint64_t uid;
+  int device;
+  bool operator==(const PoolKey& o) const { return uid == o.uid && device == o.device; }
+};
+struct PoolKeyHash {
+  size_t operator()(const PoolKey& k) const { return std::hash<uint64_t>()(k.uid * 131 + (uint64_t)k.device); }
+};
+
+struct ThreadPools {
+  std::unordered_map<PoolKey, ThreadPool, PoolKeyHash> pools;
+  ~ThreadPools() {
+    // return this thread's contexts: free them if their model is still alive
+    Registry* r = registry();
+    std::lock_guard<std::mutex> lk(r->mu);
+    for (auto& kv : pools) {
+      auto it = r->live.find(kv.first.uid);
+      if (it == r->live.end()) continue;
+      Model* m = it->second;
+      std::lock_guard<std::mutex> mlk(m->mu);
+      for (ExecCtx* c : kv.second.ctxs) {
+        auto pos = std::find(m->all_ctxs.begin(), m->all_ctxs.end(), c);
+        if (pos != m->all_ctxs.end()) {
+          m->all_ctxs.erase(pos);
+          destroy_ctx(c);
+        }
+      }
+    }
+  }
+};
+static thread_local ThreadPools t_pools;
+
+static ThreadPool& pool_of(Model* m, int dev) { return t_pools.pools[PoolKey{m->uid, dev}]; }
+
+// ---------------------------------------------------------------------------
+// replica creation: upload weights and derived layouts
+// ---------------------------------------------------------------------------
+static int make_replica(Model* m, int dev, Replica** out) {
+  for (auto& r : m->replicas)
+    if (r->device == dev) {
+      *out = r.get();
+      return ST_OK;
+    }
+  DeviceGuard guard(dev);
+  auto rep = std::make_unique<Replica>();
+  rep->device = dev;
+  cudaDeviceProp prop;
+  CUDA_TRY(cudaGetDeviceProperties(&prop, dev));
+  rep->sm_count = prop.multiProcessorCount;
+  if (prop.major != 10) {
+    set_error("forgetune_b200 kernels are built for sm_100a (B200); device " + std::to_string(dev) + " is sm_" +
+              std::to_string(prop.major) + std::to_string(prop.minor));
+    return ST_DEVICE;
+  }
+  const Graph& g = m->prog.graph;
+  std::vector<float> host(g.weights);
+  auto append = [&](size_t floats, size_t align_floats) {
+    size_t off = (host.size() + align_floats - 1) / align_floats * align_floats;
+    host.resize(off + floats, 0.0f);
+    return off;
+  };
+  rep->steps = m->prog.steps;
+  rep->conv.resize(rep->steps.size());
+  rep->tc.resize(rep->steps.size());
+  std::vector<uint64_t> ktab_off(rep->steps.size(), 0);
+  for (size_t i = 0; i < rep->steps.size(); ++i) {
+    Step& s = rep->steps[i];
+    if (s.kind == ST_GEMM) {
+      s.w_kn = s.b.offset;
+      if (m->allow_tc && tc_gemm_supported(s.K, s.N)) {
+        // W[K,N] -> W^T [N, Kp] as tf32 hi and lo parts
+        const int64_t Kp = tc_padded_k(s.K);
+        s.Kp = Kp;
+        const size_t hi = append((size_t)s.N * Kp, 64);
+        const size_t lo = append((size_t)s.N * Kp, 64);
+        const float* w = g.weights.data() + s.b.offset;
+        for (int64_t k = 0; k < s.K; ++k)
+          for (int64_t n = 0; n < s.N; ++n) {
+            const float v = w[k * s.N + n];
+            const float h = tf32_round_host(v);
+            host[hi + n * Kp + k] = h;
+            host[lo + n * Kp + k] = v - h;
+          }
+        s.w_nk_hi = hi;
+        s.w_nk_lo = lo;
+      }
+    } else if (s.kind == ST_CONV) {
+      // OIHW [Cout, K] -> B[K, Cout]
+      const size_t off = append((size_t)s.K * s.N, 16);
+      const float* w = g.weights.data() + s.b.offset;
+      for (int64_t co = 0; co < s.N; ++co)
+        for (int64_t k = 0; k < s.K; ++k) host[off + k * s.N + co] = w[co * s.K + k];
+      s.w_kn = off;
+      // k -> (input offset, dh*kh, dw*kw)
+      ktab_off[i] = append((size_t)s.K * 4, 16);
+      int32_t* t = reinterpret_cast<int32_t*>(host.data() + ktab_off[i]);
+      int64_t k = 0;
+      for (int64_t ci = 0; ci < s.Cin; ++ci)
+        for (int64_t kh = 0; kh < s.Kh; ++kh)
+          for (int64_t kw = 0; kw < s.Kw; ++kw, ++k) {
+            t[4 * k + 0] = (int32_t)(ci * s.H * s.W + kh * s.conv.dh * s.W + kw * s.conv.dw);
+            t[4 * k + 1] = (int32_t)(kh * s.conv.dh);
+            t[4 * k + 2] = (int32_t)(kw * s.conv.dw);
+            t[4 * k + 3] = 0;
+          }
+    }
+  }
+  rep->weight_floats = host.size();
+  CUDA_TRY(cudaMalloc(&rep->weights, std::max<size_t>(host.size(), 1) * sizeof(float)));
+  CUDA_TRY(cudaMemcpy(rep->weights, host.data(), host.size() * sizeof(float), cudaMemcpyHostToDevice));
+  for (size_t i = 0; i < rep->steps.size(); ++i) {
+    const Step& s = rep->steps[i];
+    if (s.kind == ST_CONV) {
+      ConvGeom c;
+      c.Cin = (int)s.Cin; c.H = (int)s.H; c.W = (int)s.W; c.Cout = (int)s.Cout;
+      c.Kh = (int)s.Kh; c.Kw = (int)s.Kw; c.Ho = (int)s.Ho; c.Wo = (int)s.Wo;
+      c.sh = (int)s.conv.sh; c.sw = (int)s.conv.sw; c.ph = (int)s.conv.ph;
+      c.pw = (int)s.conv.pw; c.dh = (int)s.conv.dh; c.dw = (int)s.conv.dw;
+      c.ktab = reinterpret_cast<const int4*>(rep->weights + ktab_off[i]);
+      rep->conv[i] = c;
+    }
+    if (s.kind == ST_GEMM && s.w_nk_hi) {
+      rep->tc[i].hi = rep->weights + s.w_nk_hi;
+      rep->tc[i].lo = rep->weights + s.w_nk_lo;
+      rep->tc[i].Kp = s.Kp;
+    }
+  }
+  *out = rep.get();
+  m->replicas.push_back(std::move(rep));
+  return ST_OK;
+}
+
+// ---------------------------------------------------------------------------
+// execution contexts
+// ---------------------------------------------------------------------------
+static constexpr int kMaxChunks = 64;
+
+static int alloc_block(ExecCtx* c, size_t bytes) {
+  if (c->block) {
+    cudaFree(c->block);
+    c->block = nullptr;
+    c->block_bytes = 0;
+  }
+  cudaError_t e = cudaMalloc(&c->block, std::max<size_t>(bytes, 256));
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    set_error(std::string("device arena allocation of ") + std::to_string(bytes) + " bytes failed: " +
+              cudaGetErrorString(e));
+    c->block = nullptr;
+    return ST_ALLOC;
+  }
+  c->block_bytes = bytes;
+  return ST_OK;
+}
+
+static size_t round256(size_t v) { return (v + 255) / 256 * 256; }
+
+static int layout_block(Model* m, ExecCtx* c, size_t min_bytes, bool* did_alloc) {
+  const Program& p = m->prog;
+  const size_t arena = round256(p.plan.arena_bytes);
+  const size_t in_b = round256((size_t)p.max_batch * p.in_static_elems * sizeof(float));
+  const size_t out_rows = p.output_dynamic ? (size_t)p.max_batch : 1;
+  const size_t out_b = round256(out_rows * p.out_static_elems * sizeof(float));
+  const size_t need = std::max(arena + in_b + out_b, min_bytes);
+  if (!c->block || c->block_bytes < need) {
+    int rc = alloc_block(c, need);
+    if (rc) return rc;
+    if (did_alloc) *did_alloc = true;
+    for (auto& cg : c->graphs) cudaGraphExecDestroy(cg.exec);
+    c->graphs.clear();
+  }
+  c->arena = c->block;
+  c->d_in = reinterpret_cast<float*>(c->block + arena);
+  c->d_out = reinterpret_cast<float*>(c->block + arena + in_b);
+  return ST_OK;
+}
+
+// Leases a free context of this thread on `dev`, creating one if all are busy.
+static int lease(Model* m, int dev, ExecCtx** out) {
+  ThreadPool& tp = pool_of(m, dev);
+  for (ExecCtx* c : tp.ctxs)
+    if (!c->in_use) {
+      c->in_use = true;
+      *out = c;
+      return ST_OK;
+    }
+  DeviceGuard guard(dev);
+  auto* c = new ExecCtx;
+  c->device = dev;
+  tp.block_insertions++;
+  m->process_allocs++;
+  if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaStreamCreateWithFlags(&c->h2d, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaStreamCreateWithFlags(&c->d2h, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaEventCreateWithFlags(&c->ev_a, cudaEventDefault) != cudaSuccess ||
+      cudaEventCreateWithFlags(&c->ev_b, cudaEventDefault) != cudaSuccess) {
+    cudaGetLastError();
+    set_error("stream / event creation failed");
+    destroy_ctx(c);
+    return ST_DEVICE;
+  }
+  c->ev_in.resize(kMaxChunks);
+  c->ev_out.resize(kMaxChunks);
+  for (int i = 0; i < kMaxChunks; ++i) {
+    if (cudaEventCreateWithFlags(&c->ev_in[i], cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&c->ev_out[i], cudaEventDisableTiming) != cudaSuccess) {
+      cudaGetLastError();
+      set_error("event creation failed");
+      destroy_ctx(c);
+      return ST_DEVICE;
+    }
+  }
+  bool did = false;
+  int rc = layout_block(m, c, 0, &did);
+  if (rc) {
+    destroy_ctx(c);
+    return rc;
+  }
+  if (did) {
+    tp.payload_allocs++;
+    m->process_allocs++;
+  }
+  {
+    std::lock_guard<std::mutex> lk(m->mu);
+    m->all_ctxs.push_back(c);
+  }
+  tp.ctxs.push_back(c);
+  c->in_use = true;
+  *out = c;
+  return ST_OK;
+}
+
+struct LeaseGuard {
+  ExecCtx* c;
+  ~LeaseGuard() {
+    if (c) c->in_use = false;
+  }
+};
+
+// ---------------------------------------------------------------------------
+// kernel dispatch
+// ---------------------------------------------------------------------------
+template <int BM, int BN, int BK, int TM, int TN, bool EXACT, bool CONV>
+static void launch_simt(const GemmArgs& a, cudaStream_t s) {
+  constexpr int NT = (BM / TM) * (BN / TN);
+  dim3 grid((unsigned)((a.M + BM - 1) / BM), (unsigned)((a.N + BN - 1) / BN));
+  simt_gemm_kernel<BM, BN, BK, TM, TN, EXACT, CONV><<<grid, NT, 0, s>>>(a);
+}
+
+template <bool EXACT, bool CONV>
+static void dispatch_simt(const GemmArgs& a, int sm_count, cudaStream_t s) {
+  const int64_t M = a.M, N = a.N;
+  if (M <= 16) {
+    launch_simt<8, 32, 8, 1, 1, EXACT, CONV>(a, s);
+  } else if (N <= 16) {
+    launch_simt<64, 16, 8, 4, 1, EXACT, CONV>(a, s);
+  } else if (((M + 127) / 128) * ((N + 127) / 128) >= 2 * sm_count) {
+    launch_simt<128, 128, 8, 8, 8, EXACT, CONV>(a, s);
+  } else {
+    launch_simt<64, 64, 8, 4, 4, EXACT, CONV>(a, s);
+  }
+}
+
+static int ew_grid(int64_t n, int sm_count) {
+  int64_t b = (n + 255) / 256;
+  return (int)std::max<int64_t>(1, std::min<int64_t>(b, (int64_t)sm_count * 8));
+}
+
+static void copy_floats(const float* a, float* y, int64_t n, int sm, cudaStream_t s) {
+  if (n <= 0) return;
+  if (((uintptr_t)a % 16 == 0) && ((uintptr_t)y % 16 == 0) && n % 4 == 0) {
+    copy4_kernel<<<ew_grid(n / 4, sm), 256, 0, s>>>(reinterpret_cast<const float4*>(a), reinterpret_cast<float4*>(y),
+                                                  n / 4);
+  } else {
+    ew_unary_kernel<EW_COPY><<<ew_grid(n, sm), 256, 0, s>>>(a, y, n);
+  }
+}
+
+// Enqueues the launch list for `batch` rows on stream s.  With `marks`
+// (steps + 1 events) an event is recorded before every step and after the
+// last one, so per-step device times can be read back afterwards.
+static int enqueue(const Model* m, const Replica* rep, char* arena, const float* in, float* out, int64_t batch,
+                   cudaStream_t s, cudaEvent_t* marks = nullptr) {
+  const int policy = m->prog.graph.kernel_policy;
+  const bool exact = policy == KP_SIMT_EXACT;
+  auto ptr = [&](const Operand& o) -> float* {
+    switch (o.space) {
+      case SP_INPUT: return const_cast<float*>(in);
+      case SP_OUTPUT: return out;
+      case SP_ARENA: return reinterpret_cast<float*>(arena + o.offset);
+      case SP_WEIGHT: return rep->weights + o.offset;
+      default: return nullptr;
+    }
+  };
+  const int sm = rep->sm_count;
+  for (size_t i = 0; i < rep->steps.size(); ++i) {
+    const Step& st = rep->steps[i];
+    const int64_t rows = st.static_rows ? 1 : batch;
+    if (marks) cudaEventRecord(marks[i], s);
+    switch (st.kind) {
+      case ST_GEMM:
+      case ST_CONV: {
+        GemmArgs a{};
+        a.A = ptr(st.a);
+        a.B = st.kind == ST_CONV ? rep->weights + st.w_kn : ptr(st.b);
+        a.bias = st.bias.space ? ptr(st.bias) : nullptr;
+        a.res = st.res.space ? ptr(st.res) : nullptr;
+        a.Y = ptr(st.out);
+        a.N = (int)st.N;
+        a.K = (int)st.K;
+        a.epi = st.epi;
+        const int64_t M = st.kind == ST_CONV ? (st.static_rows ? st.rows_per_sample : batch) * st.Ho * st.Wo
+                                             : (st.static_rows ? st.rows_per_sample : batch);
+        a.M = (int)M;
+        if (st.kind == ST_CONV) {
+          a.conv = rep->conv[i];
+          if (exact)
+            dispatch_simt<true, true>(a, sm, s);
+          else
+            dispatch_simt<false, true>(a, sm, s);
+        } else {
+          const TcWeights& tw = rep->tc[i];
+          const bool tc_ok = tw.hi != nullptr && !exact &&
+                             (policy == KP_TCGEN05 || (policy == KP_AUTO && tc_gemm_profitable(M, st.K, st.N)));
+          if (tc_ok) {
+            TcArgs t{};
+            t.A = a.A;
+            t.w_hi = tw.hi;
+            t.w_lo = tw.lo;
+            t.bias = a.bias;
+            t.res = a.res;
+            t.Y = a.Y;
+            t.M = M;
+            t.N = st.N;
+            t.K = st.K;
+            t.Kp = tw.Kp;
+            t.epi = st.epi;
+            int rc = launch_tc_gemm(t, sm, s);
+            if (rc) {
+              set_error("tensor-core GEMM launch rejected its arguments");
+              return ST_DEVICE;
+            }
+          } else if (exact) {
+            dispatch_simt<true, false>(a, sm, s);
+          } else {
+            dispatch_simt<false, false>(a, sm, s);
+          }
+        }
+        break;
+      }
+      case ST_ADD_SAME:
+      case ST_ADD_ROW:
+      case ST_ADD_CHANNEL:
+      case ST_MUL_SAME:
+      case ST_MUL_ROW:
+      case ST_MUL_CHANNEL: {
+        const int64_t n = rows * st.elems_per_sample;
+        if (n <= 0) break;
+        const float* A = ptr(st.a);
+        const float* B = ptr(st.b);
+        float* Y = ptr(st.out);
+        const int g = ew_grid(n, sm);
+        switch (st.kind) {
+          case ST_ADD_SAME: ew_binary_kernel<EW_ADD, BC_SAME><<<g, 256, 0, s>>>(A, B, Y, n, 1, 1); break;
+          case ST_ADD_ROW: ew_binary_kernel<EW_ADD, BC_ROW><<<g, 256, 0, s>>>(A, B, Y, n, st.row_len, 1); break;
+          case ST_ADD_CHANNEL:
+            ew_binary_kernel<EW_ADD, BC_CHANNEL><<<g, 256, 0, s>>>(A, B, Y, n, st.row_len, st.channels);
+            break;
+          case ST_MUL_SAME: ew_binary_kernel<EW_MUL, BC_SAME><<<g, 256, 0, s>>>(A, B, Y, n, 1, 1); break;
+          case ST_MUL_ROW: ew_binary_kernel<EW_MUL, BC_ROW><<<g, 256, 0, s>>>(A, B, Y, n, st.row_len, 1); break;
+          default:
+            ew_binary_kernel<EW_MUL, BC_CHANNEL><<<g, 256, 0, s>>>(A, B, Y, n, st.row_len, st.channels);
+            break;
+        }
+        break;
+      }
+      case ST_RELU:
+      case ST_SIGMOID:
+      case ST_TANH: {
+        const int64_t n = rows * st.elems_per_sample;
+        if (n <= 0) break;
+        const int g = ew_grid(n, sm);
+        if (st.kind == ST_RELU)
+          ew_unary_kernel<EW_RELU><<<g, 256, 0, s>>>(ptr(st.a), ptr(st.out), n);
+        else if (st.kind == ST_SIGMOID)
+          ew_unary_kernel<EW_SIGMOID><<<g, 256, 0, s>>>(ptr(st.a), ptr(st.out), n);
+        else
+          ew_unary_kernel<EW_TANH><<<g, 256, 0, s>>>(ptr(st.a), ptr(st.out), n);
+        break;
+      }
+      case ST_COPY:
+      case ST_FILL_CONST: {
+        const float* A = ptr(st.a);
+        float* Y = ptr(st.out);
+        if (A != Y) copy_floats(A, Y, rows * st.elems_per_sample, sm, s);
+        break;
+      }
+      default:
+        set_error("internal: unknown step kind");
+        return ST_DEVICE;
+    }
+  }
+  if (marks) cudaEventRecord(marks[rep->steps.size()], s);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_error(std::string("kernel launch failed: ") + cudaGetErrorString(e));
+    return ST_DEVICE;
+  }
+  return ST_OK;
+}
+
+static constexpr size_t kMaxGraphs = 16;
+
+// Replays the launch list for (batch, in, out) as a cached CUDA graph.
+static int run_graph(Model* m, Replica* rep, ExecCtx* c, const float* in, float* out, int64_t batch,
+                     cudaStream_t s) {
+  for (auto& g : c->graphs)
+    if (g.batch == batch && g.in == in && g.out == out) {
+      CUDA_TRY(cudaGraphLaunch(g.exec, s));
+      return ST_OK;
+    }
+  cudaGraph_t graph = nullptr;
+  CUDA_TRY(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
+  int rc = enqueue(m, rep, c->arena, in, out, batch, c->stream);
+  cudaError_t e = cudaStreamEndCapture(c->stream, &graph);
+  if (rc) {
+    if (graph) cudaGraphDestroy(graph);
+    return rc;
+  }
+  if (e != cudaSuccess) {
+    set_error(std::string("graph capture failed: ") + cudaGetErrorString(e));
+    return ST_DEVICE;
+  }
+  cudaGraphExec_t exec = nullptr;
+  e = cudaGraphInstantiate(&exec, graph, 0);
+  cudaGraphDestroy(graph);
+  if (e != cudaSuccess) {
+    set_error(std::string("graph instantiate failed: ") + cudaGetErrorString(e));
+    return ST_DEVICE;
+  }
+  if (c->graphs.size() >= kMaxGraphs) {
+    cudaGraphExecDestroy(c->graphs.front().exec);
+    c->graphs.erase(c->graphs.begin());
+  }
+  c->graphs.push_back({batch, in, out, exec});
+  CUDA_TRY(cudaGraphLaunch(exec, s));
+  return ST_OK;
+}
+
+static int resolve_devices(Model* m, std::vector<int>* devs) {
+  if (!m->devices.empty()) {
+    *devs = m->devices;
+    return ST_OK;
+  }
+  int d = 0;
+  CUDA_TRY(cudaGetDevice(&d));
+  devs->assign(1, d);
+  return ST_OK;
+}
+
+// rows per pipeline chunk so one chunk's input is about 32 MiB
+static int64_t chunk_rows_for(const Program& p, int64_t batch) {
+  const int64_t per_row = std::max<int64_t>(1, p.in_static_elems * 4);
+  int64_t rows = std::max<int64_t>(4096, (32ll << 20) / per_row);
+  rows = std::max<int64_t>(rows, (batch + kMaxChunks - 1) / kMaxChunks);
+  return rows;
+}
+
+// Host buffers in, host buffers out, on one device: chunked pipeline
+// H2D(c) || compute(c-1) || D2H(c-2) over three streams.
+static int run_host_one(Model* m, int dev, const float* in, float* out, int64_t batch) {
+  Replica* rep = nullptr;
+  int rc;
+  {
+    std::lock_guard<std::mutex> lk(m->mu);
+    rc = make_replica(m, dev, &rep);
+  }
+  if (rc) return rc;
+  ExecCtx* c = nullptr;
+  rc = lease(m, dev, &c);
+  if (rc) return rc;
+  LeaseGuard lg{c};
+  DeviceGuard guard(dev);
+  const Program& p = m->prog;
+  const bool chunked = p.dynamic && p.output_dynamic && batch > chunk_rows_for(p, batch);
+  if (!chunked) {
+    const size_t in_b = (size_t)(p.dynamic ? batch : 1) * p.in_static_elems * 4;
+    const size_t out_b = (size_t)(p.output_dynamic ? batch : 1) * p.out_static_elems * 4;
+    CUDA_TRY(cudaMemcpyAsync(c->d_in, in, in_b, cudaMemcpyHostToDevice, c->stream));
+    rc = run_graph(m, rep, c, c->d_in, c->d_out, batch, c->stream);
+    if (rc) return rc;
+    CUDA_TRY(cudaMemcpyAsync(out, c->d_out, out_b, cudaMemcpyDeviceToHost, c->stream));
+    CUDA_TRY(cudaStreamSynchronize(c->stream));
+    return ST_OK;
+  }
+  const int64_t cr = chunk_rows_for(p, batch);
+  const int64_t nch = (batch + cr - 1) / cr;
+  const int64_t fi = p.in_static_elems, fo = p.out_static_elems;
+  for (int64_t k = 0; k < nch; ++k) {
+    const int64_t r0 = k * cr, r1 = std::min(batch, r0 + cr);
+    CUDA_TRY(cudaMemcpyAsync(c->d_in + r0 * fi, in + r0 * fi, (size_t)(r1 - r0) * fi * 4, cudaMemcpyHostToDevice,
+                             c->h2d));
+    CUDA_TRY(cudaEventRecord(c->ev_in[k], c->h2d));
+  }
+  for (int64_t k = 0; k < nch; ++k) {
+    const int64_t r0 = k * cr, r1 = std::min(batch, r0 + cr);
+    CUDA_TRY(cudaStreamWaitEvent(c->stream, c->ev_in[k], 0));
+    rc = run_graph(m, rep, c, c->d_in + r0 * fi, c->d_out + r0 * fo, r1 - r0, c->stream);
+    if (rc) return rc;
+    CUDA_TRY(cudaEventRecord(c->ev_out[k], c->stream));
+    CUDA_TRY(cudaStreamWaitEvent(c->d2h, c->ev_out[k], 0));
+    CUDA_TRY(cudaMemcpyAsync(out + r0 * fo, c->d_out + r0 * fo, (size_t)(r1 - r0) * fo * 4,
+                             cudaMemcpyDeviceToHost, c->d2h));
+  }
+  CUDA_TRY(cudaStreamSynchronize(c->d2h));
+  CUDA_TRY(cudaStreamSynchronize(c->stream));
+  return ST_OK;
+}
+
+static int run_host(Model* m, const float* in, float* out, int64_t batch) {
+  std::vector<int> devs;
+  int rc = resolve_devices(m, &devs);
+  if (rc) return rc;
+  const Program& p = m->prog;
+  if (devs.size() == 1 || !p.dynamic || !p.output_dynamic || batch < (int64_t)devs.size()) {
+    return run_host_one(m, devs[0], in, out, batch);
+  }
+  // contiguous row blocks, one per device; the host thread drives them in turn
+  const int64_t G = (int64_t)devs.size();
+  const int64_t per = (batch + G - 1) / G;
+  std::vector<std::thread> workers;
+  std::vector<int> rcs(devs.size(), 0);
+  std::vector<std::string> errs(devs.size());
+  for (int64_t g = 0; g < G; ++g) {
+    const int64_t r0 = g * per, r1 = std::min(batch, r0 + per);
+    if (r1 <= r0) continue;
+    workers.emplace_back([&, g, r0, r1]() {
+      rcs[g] = run_host_one(m, devs[g], in + r0 * p.in_static_elems, out + r0 * p.out_static_elems, r1 - r0);
+      if (rcs[g]) errs[g] = t_last_error;
+    });
+  }
+  for (auto& w : workers) w.join();
+  for (size_t g = 0; g < rcs.size(); ++g)
+    if (rcs[g]) {
+      set_error("device " + std::to_string(devs[g]) + ": " + errs[g]);
+      return rcs[g];
+    }
+  return ST_OK;
+}
+
+// Reference validation for the three run entry points (src/codegen.cpp:722-1040).
+// api: 0 = forgetune_run, 1 = forgetune_run_v1, 2 = forgetune_run_v2.
+static int validate(const Program& p, const float* in, size_t in_count, const float* out, size_t out_count,
+                    int64_t* batch, int api) {
+  if (p.dynamic) {
+    if (api == 2 && *batch <= 0) return ST_INPUT;
+    if (api == 1) *batch = -1;
+    if (!in || !out) return ST_NULL;
+    const int64_t si = p.in_static_elems;
+    if (*batch <= 0) {
+      if (si == 0 || in_count == 0 || in_count % (size_t)si != 0) return ST_INPUT;
+      *batch = (int64_t)(in_count / (size_t)si);
+    }
+    if (*batch <= 0 || *batch > p.max_batch) return ST_INPUT;
+    if (in_count != (size_t)(*batch * si)) return ST_INPUT;
+    const size_t want_out = p.output_dynamic ? (size_t)(*batch * p.out_static_elems) : (size_t)p.out_static_elems;
+    if (out_count != want_out) return ST_OUTPUT;
+    return ST_OK;
+  }
+  if (api == 2 && (*batch <= 0 || *batch != p.static_batch)) return ST_INPUT;
+  if (!in || !out) return ST_NULL;
+  if (in_count != (size_t)p.in_static_elems) return ST_INPUT;
+  if (out_count != (size_t)p.out_static_elems) return ST_OUTPUT;
+  *batch = p.static_batch;
+  return ST_OK;
+}
+
+}  // namespace ftb
+
+using namespace ftb;
+
+// ===========================================================================
+// C ABI
+// ===========================================================================
+FTB_API const char* ftb_last_error(void) { return t_last_error.c_str(); }
+
+FTB_API int ftb_describe_blob(const void* blob, size_t bytes, char* buf, size_t cap) {
+  try {
+    Program p = build_program(blob, bytes);
+    std::string s = p.describe();
+    if (buf && cap) {
+      size_t n = std::min(cap - 1, s.size());
+      std::memcpy(buf, s.data(), n);
+      buf[n] = 0;
+    }
+    return (int)s.size();
+  } catch (const std::exception& e) {
+    set_error(e.what());
+    return ST_CONFIG;
+  }
+}
+
+FTB_API int ftb_model_create(const void* blob, size_t bytes, void** out_model) {
+  if (!blob || !out_model) return ST_NULL;
+  try {
+    auto* m = new Model;
+    m->prog = build_program(blob, bytes);
+    Registry* r = registry();
+    m->uid = r->next_uid++;
+    {
+      std::lock_guard<std::mutex> lk(r->mu);
+      r->live[m->uid] = m;
+    }
+    *out_model = m;
+    return ST_OK;
+  } catch (const std::exception& e) {
+    set_error(e.what());
+    return ST_CONFIG;
+  }
+}
+
+FTB_API void ftb_model_destroy(void* handle) {
+  auto* m = static_cast<Model*>(handle);
+  if (!m) return;
+  Registry* r = registry();
+  {
+    std::lock_guard<std::mutex> lk(r->mu);
+    r->live.erase(m->uid);
+  }
+  for (ExecCtx* c : m->all_ctxs) destroy_ctx(c);
+  m->all_ctxs.clear();
+  for (auto& rep : m->replicas) {
+    DeviceGuard g(rep->device);
+    if (rep->weights) cudaFree(rep->weights);
+  }
+  m->replicas.clear();
+  delete m;
+}
+
+FTB_API int ftb_model_set_devices(void* handle, const int* ids, int n) {
+  auto* m = static_cast<Model*>(handle);
+  if (!m || (n > 0 && !ids)) return ST_NULL;
+  int count = 0;
+  CUDA_TRY(cudaGetDeviceCount(&count));
+  std::vector<int> d;
+  for (int i = 0; i < n; ++i) {
+    if (ids[i] < 0 || ids[i] >= count) {
+      set_error("device id " + std::to_string(ids[i]) + " out of range");
+      return ST_CONFIG;
+    }
+    d.push_back(ids[i]);
+  }
+  std::lock_guard<std::mutex> lk(m->mu);
+  m->devices = d;
+  return ST_OK;
+}
+
+FTB_API int ftb_model_set_policy(void* handle, int policy) {
+  auto* m = static_cast<Model*>(handle);
+  if (!m) return ST_NULL;
+  if (policy < KP_AUTO || policy > KP_TCGEN05) return ST_CONFIG;
+  std::lock_guard<std::mutex> lk(m->mu);
+  m->prog.graph.kernel_policy = policy;
+  for (ExecCtx* c : m->all_ctxs) {
+    for (auto& cg : c->graphs) cudaGraphExecDestroy(cg.exec);
+    c->graphs.clear();
+  }
+  return ST_OK;
+}
+
+FTB_API int ftb_model_prepare(void* handle) {
+  auto* m = static_cast<Model*>(handle);
+  if (!m) return ST_NULL;
+  std::vector<int> devs;
+  int rc = resolve_devices(m, &devs);
+  if (rc) return rc;
+  for (int d : devs) {
+    Replica* rep = nullptr;
+    {
+      std::lock_guard<std::mutex> lk(m->mu);
+      rc = make_replica(m, d, &rep);
+    }
+    if (rc) return rc;
+    ExecCtx* c = nullptr;
+    rc = lease(m, d, &c);
+    if (rc) return rc;
+    c->in_use = false;
+  }
+  return ST_OK;
+}
+
+FTB_API int ftb_model_run(void* handle, const float* in, size_t in_count, float* out, size_t out_count,
+                          int64_t batch, int api) {
+  auto* m = static_cast<Model*>(handle);
+  if (!m) return ST_NULL;
+  int rc = validate(m->prog, in, in_count, out, out_count, &batch, api);
+  if (rc) return rc;
+  try {
+    return run_host(m, in, out, batch);
+  } catch (const std::exception& e) {
+    set_error(e.what());
+    return ST_ALLOC;
+  }
+}
+
+FTB_API int ftb_model_run_device(void* handle, const float* d_in, size_t in_count, float* d_out, size_t out_count,
+                                 int64_t batch, void* stream) {
+  auto* m = static_cast<Model*>(handle);
+  if (!m) return ST_NULL;
+  int rc = validate(m->prog, d_in, in_count, d_out, out_count, &batch, 2);
+  if (rc) return rc;
+  std::vector<int> devs;
+  rc = resolve_devices(m, &devs);
+  if (rc) return rc;
+  const int dev = devs[0];
+  Replica* rep = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(m->mu);
+    rc = make_replica(m, dev, &rep);
+  }
+  if (rc) return rc;
+  ExecCtx* c = nullptr;
+  rc = lease(m, dev, &c);
+  if (rc) return rc;
+  LeaseGuard lg{c};
+  DeviceGuard guard(dev);
+  cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : c->stream;
+  return run_graph(m, rep, c, d_in, d_out, batch, s);
+}
+
+static constexpr int kProfSlots = 1024;
+
+// Like ftb_model_run_device, but launches the steps directly (no graph) with
+// an event before every step and after the last, kept in `slot` of the
+// calling thread's context until ftb_model_profile_read.
+FTB_API int ftb_model_run_device_profiled(void* handle, const float* d_in, size_t in_count, float* d_out,
+                                          size_t out_count, int64_t batch, void* stream, int slot) {
+  auto* m = static_cast<Model*>(handle);
+  if (!m) return ST_NULL;
+  if (slot < 0 || slot >= kProfSlots) {
+    set_error("profile slot out of range");
+    return ST_CONFIG;
+  }
+  int rc = validate(m->prog, d_in, in_count, d_out, out_count, &batch, 2);
+  if (rc) return rc;
+  std::vector<int> devs;
+  rc = resolve_devices(m, &devs);
+  if (rc) return rc;
+  Replica* rep = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(m->mu);
+    rc = make_replica(m, devs[0], &rep);
+  }
+  if (rc) return rc;
+  ExecCtx* c = nullptr;
+  rc = lease(m, devs[0], &c);
+  if (rc) return rc;
+  LeaseGuard lg{c};
+  DeviceGuard guard(devs[0]);
+  const size_t per = rep->steps.size() + 1;
+  const size_t need = per * (size_t)(slot + 1);
+  while (c->prof.size() < need) {
+    cudaEvent_t e;
+    CUDA_TRY(cudaEventCreate(&e));
+    c->prof.push_back(e);
+  }
+  cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : c->stream;
+  return enqueue(m, rep, c->arena, d_in, d_out, batch, s, c->prof.data() + per * slot);
+}
+
+// Waits for the events of `slot` and writes each step's device time (ms).
+// Returns the number of steps, or a negative status.
+FTB_API int ftb_model_profile_read(void* handle, int slot, float* step_ms, int cap) {
+  auto* m = static_cast<Model*>(handle);
+  if (!m || !step_ms) return ST_NULL;
+  std::vector<int> devs;
+  int rc = resolve_devices(m, &devs);
+  if (rc) return rc;
+  ExecCtx* c = nullptr;
+  rc = lease(m, devs[0], &c);
+  if (rc) return rc;
+  LeaseGuard lg{c};
+  DeviceGuard guard(devs[0]);
+  const size_t n = m->prog.steps.size();
+  const size_t per = n + 1;
+  if (slot < 0 || per * (size_t)(slot + 1) > c->prof.size()) {
+    set_error("profile slot was never recorded on this thread");
+    return ST_CONFIG;
+  }
+  for (size_t i = 0; i < n && (int)i < cap; ++i) {
+    CUDA_TRY(cudaEventSynchronize(c->prof[per * slot + i + 1]));
+    float ms = 0.0f;
+    CUDA_TRY(cudaEventElapsedTime(&ms, c->prof[per * slot + i], c->prof[per * slot + i + 1]));
+    step_ms[i] = ms;
+  }
+  return (int)n;
+}
+
+FTB_API double ftb_model_benchmark(void* handle, const float* in, size_t in_count, float* out, size_t out_count,
+                                   int iters) {
+  auto* m = static_cast<Model*>(handle);
+  if (!m || !in || !out || iters <= 0) return -1.0;
+  const Program& p = m->prog;
+  int64_t batch;
+  if (p.dynamic) {
+    const int64_t si = p.in_static_elems;
+    if (si == 0 || in_count == 0 || in_count % (size_t)si != 0) return -2.0;
+    batch = (int64_t)(in_count / (size_t)si);
+    if (batch <= 0 || batch > p.max_batch) return -2.0;
+    const size_t want_out = p.output_dynamic ? (size_t)(batch * p.out_static_elems) : (size_t)p.out_static_elems;
+    if (out_count != want_out) return -3.0;
+  } else {
+    if (in_count != (size_t)p.in_static_elems) return -2.0;
+    if (out_count != (size_t)p.out_static_elems) return -3.0;
+    batch = p.static_batch;
+  }
+  std::vector<int> devs;
+  if (resolve_devices(m, &devs)) return -4.0;
+  const int dev = devs[0];
+  Replica* rep = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(m->mu);
+    if (make_replica(m, dev, &rep)) return -4.0;
+  }
+  ExecCtx* c = nullptr;
+  if (lease(m, dev, &c)) return -4.0;
+  LeaseGuard lg{c};
+  DeviceGuard guard(dev);
+  const size_t in_b = in_count * 4, out_b = out_count * 4;
+  if (cudaMemcpyAsync(c->d_in, in, in_b, cudaMemcpyHostToDevice, c->stream) != cudaSuccess) return -5.0;
+  for (int w = 0; w < 10; ++w)
+    if (run_graph(m, rep, c, c->d_in, c->d_out, batch, c->stream)) return -5.0;
+  if (cudaEventRecord(c->ev_a, c->stream) != cudaSuccess) return -5.0;
+  for (int i = 0; i < iters; ++i)
+    if (run_graph(m, rep, c, c->d_in, c->d_out, batch, c->stream)) return -5.0;
+  if (cudaEventRecord(c->ev_b, c->stream) != cudaSuccess) return -5.0;
+  if (cudaMemcpyAsync(out, c->d_out, out_b, cudaMemcpyDeviceToHost, c->stream) != cudaSuccess) return -5.0;
+  if (cudaStreamSynchronize(c->stream) != cudaSuccess) return -5.0;
+  float ms = 0.0f;
+  if (cudaEventElapsedTime(&ms, c->ev_a, c->ev_b) != cudaSuccess) return -5.0;
+  return (double)ms * 1000.0 / iters;
+}
+
+FTB_API int ftb_model_is_dynamic(void* handle) {
+  auto* m = static_cast<Model*>(handle);
+  return m && m->prog.dynamic ? 1 : 0;
+}
+
+FTB_API int64_t ftb_model_max_batch(void* handle) {
+  auto* m = static_cast<Model*>(handle);
+  return m ? m->prog.max_batch : 0;
+}
+
+// which: 0 total (payload + insertions), 1 payload, 2 insertions, 3 process total
+FTB_API size_t ftb_model_counter(void* handle, int which) {
+  auto* m = static_cast<Model*>(handle);
+  if (!m) return 0;
+  if (which == 3) return m->process_allocs.load();
+  size_t payload = 0, ins = 0;
+  for (auto& kv : t_pools.pools)
+    if (kv.first.uid == m->uid) {
+      payload += kv.second.payload_allocs;
+      ins += kv.second.block_insertions;
+    }
+  return which == 1 ? payload : which == 2 ? ins : payload + ins;
+}
+
+FTB_API void ftb_model_reset_counters(void* handle) {
+  auto* m = static_cast<Model*>(handle);
+  if (!m) return;
+  for (auto& kv : t_pools.pools)
+    if (kv.first.uid == m->uid) {
+      kv.second.payload_allocs = 0;
+      kv.second.block_insertions = 0;
+    }
+}
+
+// Forces a 64 MiB arena allocation in this thread's pool (the reference's
+// forgetune_test_inject_arena_alloc, src/codegen.cpp:1125-1130).
+FTB_API void ftb_model_inject_alloc(void* handle) {
+  auto* m = static_cast<Model*>(handle);
+  if (!m) return;
+  std::vector<int> devs;
+  if (resolve_devices(m, &devs)) return;
+  ExecCtx* c = nullptr;
+  if (lease(m, devs[0], &c)) return;
+  LeaseGuard lg{c};
+  DeviceGuard guard(c->device);
+  if (layout_block(m, c, c->block_bytes + (64u << 20), nullptr) == ST_OK) {
+    pool_of(m, devs[0]).payload_allocs++;
+    m->process_allocs++;
+  }
+}
+
+FTB_API int ftb_model_describe(void* handle, char* buf, size_t cap) {
+  auto* m = static_cast<Model*>(handle);
+  if (!m) return ST_NULL;
+  std::string s = m->prog.describe();
+  if (buf && cap) {
+    size_t n = std::min(cap - 1, s.size());
+    std::memcpy(buf, s.data(), n);
+    buf[n] = 0;
+  }
+  return (int)s.size();
+}
+
+FTB_API int ftb_device_count(void) {
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return n;
+}
+
+// Elements [first, first+count) of the Philox4x32-10 normal stream keyed by
+// seed, written to device memory d_out on `stream`.
+FTB_API int ftb_philox_normal(float* d_out, uint64_t seed, uint64_t first, uint64_t count, void* stream) {
+  if (!d_out) return ST_NULL;
+  if (count == 0) return ST_OK;
+  int dev = 0, sm = 148;
+  CUDA_TRY(cudaGetDevice(&dev));
+  cudaDeviceGetAttribute(&sm, cudaDevAttrMultiProcessorCount, dev);
+  const uint64_t blocks = (count + 3) / 4 + 1;
+  const unsigned grid = (unsigned)std::min<uint64_t>((blocks + 255) / 256, (uint64_t)sm * 16);
+  philox_normal_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(d_out, seed, first, count);
+  CUDA_TRY(cudaGetLastError());
+  return ST_OK;
+}

@@ -56,17 +56,26 @@ ORA_EXPORT void ora_gemm_bias_first(int64_t M, int64_t K, int64_t N,
     }
 }
 
-/* y[M,N] = (relu?)((sum_k x[m,k] w[k,n]) + bias) with the bias-last order. */
+/* y[M,N] = (relu?)((sum_k x[m,k] w[k,n]) + bias) with the bias-last order.
+ * Each output is 0 + x0*w0 + x1*w1 + ... in k order, then + bias: the same
+ * rounding sequence as the reference's naive i-j-k loop, evaluated here in
+ * i-k-j order so the weight rows stream through the cache. */
 ORA_EXPORT void ora_gemm_bias_last(int64_t M, int64_t K, int64_t N,
                                    const float* x, const float* w,
                                    const float* bias, int bias_rows, int relu,
                                    float* y) {
     for (int64_t i = 0; i < M; ++i) {
+        float* yr = y + i * N;
+        for (int64_t j = 0; j < N; ++j) yr[j] = 0.0f;
+        for (int64_t k = 0; k < K; ++k) {
+            const float a = x[i * K + k];
+            const float* wr = w + k * N;
+            for (int64_t j = 0; j < N; ++j) yr[j] += a * wr[j];
+        }
         for (int64_t j = 0; j < N; ++j) {
-            float sum = 0.0f;
-            for (int64_t k = 0; k < K; ++k) sum += x[i * K + k] * w[k * N + j];
+            float sum = yr[j];
             if (bias) sum += bias_rows ? bias[i * N + j] : bias[j];
-            y[i * N + j] = relu ? ora_relu1(sum) : sum;
+            yr[j] = relu ? ora_relu1(sum) : sum;
         }
     }
 }

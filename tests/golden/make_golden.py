@@ -100,9 +100,24 @@ def ref_run(so_path: str, x: np.ndarray, out_feats: int) -> np.ndarray:
     return y
 
 
+def reference_plan(name: str) -> dict:
+    """Arena size and buffer offsets the reference planner chose, read from the
+    kernel.cpp its code generator emitted (``acquire(<bytes>)`` and
+    ``buf_<id> = arena + <float offset>`` lines, in execution order)."""
+    import re
+    path = os.path.join(REF_DIR, "_src", name, "kernel_fused_ikj.cpp")
+    with open(path) as f:
+        src = f.read()
+    arena = int(re.search(r"g_thread_arena_pool\.acquire\((\d+)\)", src).group(1))
+    offs = [int(m.group(2)) * 4 for m in re.finditer(r"float\* buf_(\d+) = arena \+ (\d+);", src)]
+    return {"arena_bytes": arena, "offsets_bytes": offs}
+
+
 def main() -> int:
     arrays = {}
-    meta = {"torch": torch.__version__, "weights_sha256": {}, "cases": []}
+    meta = {"torch": torch.__version__, "weights_sha256": {}, "cases": [], "reference_plans": {}}
+    for name in ("tiny_mlp", "residual_mlp", "small_cnn"):
+        meta["reference_plans"][name] = reference_plan(name)
     models = {}
     for name, B, kind in CASES:
         if name not in models:
