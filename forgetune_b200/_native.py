@@ -137,13 +137,13 @@ class EngineModel:
                                        x.shape[0] if self.desc["dynamic"] else 0, api))
 
     def run_device(self, d_in: int, in_count: int, d_out: int, out_count: int, batch: int, stream: int = 0) -> None:
-        self._check(lib().ftb_model_run_device(self.handle, d_in, in_count, d_out, out_count, batch, stream or None),
+        self._check(lib().ftb_model_run_device(self.handle, d_in, in_count, d_out, out_count, batch, stream),
                     "run_device")
 
     def run_device_profiled(self, d_in: int, in_count: int, d_out: int, out_count: int, batch: int,
                             stream: int, slot: int) -> None:
         self._check(lib().ftb_model_run_device_profiled(self.handle, d_in, in_count, d_out, out_count, batch,
-                                                        stream or None, slot), "run_device_profiled")
+                                                        stream, slot), "run_device_profiled")
 
     def profile_read(self, slot: int):
         n = len(self.desc["steps"])

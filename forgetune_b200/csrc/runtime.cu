@@ -83,6 +83,10 @@ struct Replica {
   std::vector<ConvGeom> conv;  // per step (valid for ST_CONV)
   std::vector<TcWeights> tc;   // per step (valid when the tensor-core path may run)
   int sm_count = 148;
+  // error word the tensor-core kernel writes when a bounded wait gives up;
+  // mapped pinned host memory, so the host reads it without a copy
+  int* err_host = nullptr;
+  int* err_dev = nullptr;
 };
 
 struct ExecCtx {
@@ -281,8 +285,12 @@ static int make_replica(Model* m, int dev, Replica** out) {
       rep->tc[i].hi = rep->weights + s.w_nk_hi;
       rep->tc[i].lo = rep->weights + s.w_nk_lo;
       rep->tc[i].Kp = s.Kp;
+      if (!tc_prepare_weights(rep->tc[i], s.N)) rep->tc[i] = TcWeights{};  // SIMT for this layer
     }
   }
+  CUDA_TRY(cudaHostAlloc(reinterpret_cast<void**>(&rep->err_host), sizeof(int), cudaHostAllocMapped));
+  *rep->err_host = 0;
+  CUDA_TRY(cudaHostGetDevicePointer(reinterpret_cast<void**>(&rep->err_dev), rep->err_host, 0));
   *out = rep.get();
   m->replicas.push_back(std::move(rep));
   return ST_OK;
@@ -478,8 +486,9 @@ static int enqueue(const Model* m, const Replica* rep, char* arena, const float*
             dispatch_simt<false, true>(a, sm, s);
         } else {
           const TcWeights& tw = rep->tc[i];
-          const bool tc_ok = tw.hi != nullptr && !exact &&
+          const bool tc_ok = tw.maps_ready && !exact &&
                              (policy == KP_TCGEN05 || (policy == KP_AUTO && tc_gemm_profitable(M, st.K, st.N)));
+          int tc_rc = 1;  // 1: not taken
           if (tc_ok) {
             TcArgs t{};
             t.A = a.A;
@@ -493,11 +502,14 @@ static int enqueue(const Model* m, const Replica* rep, char* arena, const float*
             t.K = st.K;
             t.Kp = tw.Kp;
             t.epi = st.epi;
-            int rc = launch_tc_gemm(t, sm, s);
-            if (rc) {
-              set_error("tensor-core GEMM launch rejected its arguments");
+            tc_rc = launch_tc_gemm(t, tw, rep->err_dev, sm, s);
+            if (tc_rc < 0) {
+              set_error(std::string("tensor-core GEMM launch failed: ") + cudaGetErrorString(cudaGetLastError()));
               return ST_DEVICE;
             }
+          }
+          if (tc_rc == 0) {
+            // launched on the tensor cores
           } else if (exact) {
             dispatch_simt<true, false>(a, sm, s);
           } else {
@@ -562,6 +574,16 @@ static int enqueue(const Model* m, const Replica* rep, char* arena, const float*
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
     set_error(std::string("kernel launch failed: ") + cudaGetErrorString(e));
+    return ST_DEVICE;
+  }
+  return ST_OK;
+}
+
+// After a synchronising call: did a tensor-core kernel give up on a wait?
+static int check_kernel_error(const Replica* rep) {
+  const volatile int* e = rep->err_host;
+  if (e && *e != 0) {
+    set_error("tensor-core GEMM aborted: a pipeline wait exceeded its limit (code " + std::to_string(*e) + ")");
     return ST_DEVICE;
   }
   return ST_OK;
@@ -649,7 +671,7 @@ static int run_host_one(Model* m, int dev, const float* in, float* out, int64_t 
     if (rc) return rc;
     CUDA_TRY(cudaMemcpyAsync(out, c->d_out, out_b, cudaMemcpyDeviceToHost, c->stream));
     CUDA_TRY(cudaStreamSynchronize(c->stream));
-    return ST_OK;
+    return check_kernel_error(rep);
   }
   const int64_t cr = chunk_rows_for(p, batch);
   const int64_t nch = (batch + cr - 1) / cr;
@@ -663,7 +685,8 @@ static int run_host_one(Model* m, int dev, const float* in, float* out, int64_t 
   for (int64_t k = 0; k < nch; ++k) {
     const int64_t r0 = k * cr, r1 = std::min(batch, r0 + cr);
     CUDA_TRY(cudaStreamWaitEvent(c->stream, c->ev_in[k], 0));
-    rc = run_graph(m, rep, c, c->d_in + r0 * fi, c->d_out + r0 * fo, r1 - r0, c->stream);
+    // chunks are thousands of rows: launch directly, no graph per chunk address
+    rc = enqueue(m, rep, c->arena, c->d_in + r0 * fi, c->d_out + r0 * fo, r1 - r0, c->stream);
     if (rc) return rc;
     CUDA_TRY(cudaEventRecord(c->ev_out[k], c->stream));
     CUDA_TRY(cudaStreamWaitEvent(c->d2h, c->ev_out[k], 0));
@@ -672,7 +695,7 @@ static int run_host_one(Model* m, int dev, const float* in, float* out, int64_t 
   }
   CUDA_TRY(cudaStreamSynchronize(c->d2h));
   CUDA_TRY(cudaStreamSynchronize(c->stream));
-  return ST_OK;
+  return check_kernel_error(rep);
 }
 
 static int run_host(Model* m, const float* in, float* out, int64_t batch) {
@@ -790,6 +813,7 @@ FTB_API void ftb_model_destroy(void* handle) {
   for (auto& rep : m->replicas) {
     DeviceGuard g(rep->device);
     if (rep->weights) cudaFree(rep->weights);
+    if (rep->err_host) cudaFreeHost(rep->err_host);
   }
   m->replicas.clear();
   delete m;
@@ -882,7 +906,7 @@ FTB_API int ftb_model_run_device(void* handle, const float* d_in, size_t in_coun
   if (rc) return rc;
   LeaseGuard lg{c};
   DeviceGuard guard(dev);
-  cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : c->stream;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);  // NULL: the legacy default stream
   return run_graph(m, rep, c, d_in, d_out, batch, s);
 }
 
@@ -922,7 +946,7 @@ FTB_API int ftb_model_run_device_profiled(void* handle, const float* d_in, size_
     CUDA_TRY(cudaEventCreate(&e));
     c->prof.push_back(e);
   }
-  cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : c->stream;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);  // NULL: the legacy default stream
   return enqueue(m, rep, c->arena, d_in, d_out, batch, s, c->prof.data() + per * slot);
 }
 

@@ -207,7 +207,7 @@ class NativeRuntime:
         fo = int(math.prod(self._output_shape_tail)) if self.is_output_dynamic else self.total_output_count
         ic = b * fi if self.is_dynamic else fi
         oc = b * fo if self.is_output_dynamic else fo
-        st = self.run_device_fn(d_input, ic, d_output, oc, b, stream or None)
+        st = self.run_device_fn(d_input, ic, d_output, oc, b, stream)
         if st != 0:
             self._raise_status(st, "device run, batch=%d" % b)
 

@@ -84,9 +84,10 @@ FORGETUNE_EXPORT void forgetune_test_inject_arena_alloc(void);
  * forgetune_set_devices: shard the batch over these CUDA devices (contiguous
  * row blocks, one weight replica each); call before the first run.
  * forgetune_run_v2_device: inputs/outputs in device memory of the (first)
- * configured device, enqueued on `stream` (a cudaStream_t, NULL = the
- * context's own stream) without synchronising.  Calls from one thread on
- * different streams must be ordered by the caller (they share its arena). */
+ * configured device, enqueued on `stream` (a cudaStream_t; NULL = the legacy
+ * default stream, as in CUDA libraries) without synchronising.  Calls from
+ * one thread on different streams must be ordered by the caller (they share
+ * its arena). */
 FORGETUNE_EXPORT int forgetune_create(void);
 FORGETUNE_EXPORT void forgetune_destroy(void);
 FORGETUNE_EXPORT int forgetune_set_devices(const int* device_ids, int n);

@@ -1,0 +1,65 @@
+"""The tcgen05 3xTF32 GEMM on ragged shapes: M not a multiple of the 128-row
+tile, K not a multiple of the 32-wide k-block, N not a multiple of the tile
+width or of 4, each epilogue form; against the CPU oracle with the
+reference's tolerance, and bitwise run to run."""
+
+import numpy as np
+import pytest
+import torch
+import torch.nn as nn
+
+from forgetune_b200 import compile_model
+from oracle import oracle
+
+pytestmark = pytest.mark.gpu
+
+
+class Block(nn.Module):
+    def __init__(self, k, n, relu, residual):
+        super().__init__()
+        self.fc = nn.Linear(k, n)
+        self.relu = relu
+        self.residual = residual
+
+    def forward(self, x):
+        y = self.fc(x)
+        if self.relu:
+            y = torch.relu(y)
+        if self.residual:
+            y = y + x
+        return y
+
+
+SHAPES = [
+    # M, K, N, relu, residual
+    (1000, 784, 256, True, False),
+    (257, 96, 200, False, False),
+    (4097, 512, 512, False, True),
+    (130, 36, 64, True, False),
+    (2048, 1024, 50, False, False),
+    (300, 128, 384, True, False),
+    (65536, 784, 256, True, False),
+]
+
+
+@pytest.mark.parametrize("M,K,N,relu,residual", SHAPES)
+def test_tcgen05_matches_oracle(M, K, N, relu, residual, tmp_path):
+    if residual:
+        assert K == N
+    torch.manual_seed(M + K + N)
+    m = Block(K, N, relu, residual).eval()
+    cm = compile_model(m, (torch.randn(2, K),), output_dir=str(tmp_path), autotune=False, enable_fusion=True,
+                       kernel_variant="fused_ikj", dynamic_batch=True, max_batch_size=max(M, 2),
+                       max_workspace_bytes=8 << 30, gpu_kernel="tcgen05", verify=False)
+    steps = cm.plan()["steps"]
+    assert steps[0]["K"] == K and steps[0]["N"] == N
+    x = np.random.default_rng(M).standard_normal((M, K)).astype(np.float32)
+    got = cm.run(x)
+    w = m.fc.weight.detach().numpy().T.copy()
+    want = oracle.gemm(x, w, m.fc.bias.detach().numpy(), relu=relu, order="bias_last")
+    if residual:
+        want = oracle.add(want, x)
+    assert np.allclose(got, want, atol=1e-4, rtol=1e-4), float(np.max(np.abs(got - want)))
+    again = cm.run(x)
+    assert np.array_equal(got.view(np.uint32), again.view(np.uint32))
+    cm.close()
