@@ -302,35 +302,36 @@ def run_ours(args) -> int:
         "fp32_ffma_nominal_tflops": 148 * 128 * 2 * 1.965e9 / 1e12,
     }
 
-    # end to end through the public host API, pinned host buffers
-    xh = torch.empty((B, IN_F), dtype=torch.float32, pin_memory=True)
-    xh.copy_(x.view(B, IN_F))
-    xh_np = xh.numpy()
-    rt = cm._runtime
-    for _ in range(max(1, args.warmup)):
-        rt.run(xh_np)
-    barrier()
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        out_host = rt.run(xh_np)
-    e2e_s = max_over_ranks(time.perf_counter() - t0)
-    e2e = {"value": world * B * args.steps / e2e_s, "unit": UNIT,
-           "h2d_bytes_per_step": B * IN_F * 4, "d2h_bytes_per_step": int(out_host.nbytes),
-           "ms_per_step": 1000.0 * e2e_s / args.steps}
+    e2e, p50_b1, dev_b1, base = None, None, None, None
+    if not args.quick:
+        # end to end through the public host API, pinned host buffers
+        xh = torch.empty((B, IN_F), dtype=torch.float32, pin_memory=True)
+        xh.copy_(x.view(B, IN_F))
+        xh_np = xh.numpy()
+        rt = cm._runtime
+        for _ in range(max(1, args.warmup)):
+            rt.run(xh_np)
+        barrier()
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            out_host = rt.run(xh_np)
+        e2e_s = max_over_ranks(time.perf_counter() - t0)
+        e2e = {"value": world * B * args.steps / e2e_s, "unit": UNIT,
+               "h2d_bytes_per_step": B * IN_F * 4, "d2h_bytes_per_step": int(out_host.nbytes),
+               "ms_per_step": 1000.0 * e2e_s / args.steps}
 
-    # p50 latency at B=1 through the host API (graph replay)
-    x1 = np.ascontiguousarray(xh_np[:1])
-    for _ in range(20):
-        rt.run(x1)
-    lat = []
-    for _ in range(200):
-        t0 = time.perf_counter_ns()
-        rt.run(x1)
-        lat.append((time.perf_counter_ns() - t0) / 1000.0)
-    p50_b1 = statistics.median(lat)
-    dev_b1 = cm.benchmark_kernel(iters=1000, batch_size=1)
-
-    base = cpu_baseline() if (rank == 0 and world == 1) else None
+        # p50 latency at B=1 through the host API (graph replay)
+        x1 = np.ascontiguousarray(xh_np[:1])
+        for _ in range(20):
+            rt.run(x1)
+        lat = []
+        for _ in range(200):
+            t0 = time.perf_counter_ns()
+            rt.run(x1)
+            lat.append((time.perf_counter_ns() - t0) / 1000.0)
+        p50_b1 = statistics.median(lat)
+        dev_b1 = cm.benchmark_kernel(iters=1000, batch_size=1)
+        base = cpu_baseline() if (rank == 0 and world == 1) else None
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
@@ -364,6 +365,8 @@ def main() -> int:
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--batch", type=int, default=BATCH)
     ap.add_argument("--policy", default="auto", choices=["auto", "simt", "simt_exact", "tcgen05"])
+    ap.add_argument("--quick", action="store_true",
+                    help="device-resident timing only (no e2e, latency or CPU baseline), for profiler captures")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
