@@ -241,7 +241,7 @@ static int make_replica(Model* m, int dev, Replica** out) {
             const float v = w[k * s.N + n];
             const float h = tf32_round_host(v);
             host[hi + n * Kp + k] = h;
-            host[lo + n * Kp + k] = v - h;
+            host[lo + n * Kp + k] = tf32_round_host(v - h);
           }
         s.w_nk_hi = hi;
         s.w_nk_lo = lo;

@@ -2,20 +2,27 @@
 //
 //   y[m, n] = epi( sum_k A[m, k] W[k, n] ),   A fp32 [M, K] row-major
 //
-// Every fp32 value v is split as hi = tf32_round(v) and lo = v - hi (exact),
-// and the product is accumulated in fp32 as hi_a*hi_w + hi_a*lo_w + lo_a*hi_w
-// (the lo*lo term is below fp32 resolution).  W is split once on the host and
-// stored transposed, K-major, as two [N, Kp] arrays; A is split on the fly.
+// Every fp32 value v is split as hi = tf32(v) and lo = tf32(v - hi), both
+// rounded to nearest, and the product is accumulated in fp32 as
+// hi_a*hi_w + hi_a*lo_w + lo_a*hi_w (the lo*lo term is below fp32
+// resolution).  W is split once on the host and stored transposed, K-major,
+// as two [N, Kp] arrays; A is split on the fly in shared memory.
 //
-// One CTA computes a 128 x BN tile with six warps:
-//   warp 0      TMA producer: A tile (fp32) and W_hi / W_lo tiles per k-block
-//               of 32, 128-byte swizzled, into a STAGES-deep ring;
-//   warp 1      allocates the TMEM accumulator; one thread issues
-//               tcgen05.mma (kind::tf32, M=128, N=BN, K=8) three times per
-//               k-step and tcgen05.commit frees each stage;
-//   warps 2-5   split each A tile in shared memory (hi in place, lo beside
-//               it), then run the epilogue: tcgen05.ld of the accumulator,
-//               bias / ReLU / residual, stores.
+// Persistent kernel: one CTA per SM walks a static round-robin list of
+// 128 x BN output tiles (n fastest, so CTAs working on one row block run
+// together and share its A tile through L2).  Ten warps:
+//   warp 0      TMA producer: A (fp32), W_hi and W_lo tiles per k-block of
+//               32, 128-byte swizzled, into a STAGES-deep ring that runs
+//               continuously across tiles;
+//   warp 1      allocates two TMEM accumulators (2 x BN columns); one thread
+//               issues tcgen05.mma (kind::tf32, M=128, N=BN, K=8) three times
+//               per k-step into the accumulator of the current tile and
+//               tcgen05.commit frees each stage / publishes each tile;
+//   warps 2-5   split each A tile in shared memory (hi in place, lo beside);
+//   warps 6-9   epilogue of the previous tile, overlapping the MMAs of the
+//               next: tcgen05.ld, a per-warp shared-memory transpose so each
+//               store instruction writes 128 contiguous bytes of one row,
+//               then bias / ReLU / residual.
 // Every mbarrier wait is bounded: on timeout the kernel records an error
 // code, skips the remaining work, waits (bounded) for MMAs in flight,
 // releases its TMEM and returns.
@@ -33,7 +40,7 @@ namespace ftb {
 
 struct TcWeights {
   const float* hi = nullptr;  // W^T [N, Kp], tf32-rounded
-  const float* lo = nullptr;  // W^T - hi
+  const float* lo = nullptr;  // tf32(W^T - hi)
   int64_t Kp = 0;
   CUtensorMap map_hi[3];      // one per supported BN (64, 128, 256)
   CUtensorMap map_lo[3];
@@ -57,12 +64,12 @@ struct TcKernelParams {
   float* Y;
   int M, N, K;
   uint32_t epi;
-  int vec_store;  // Y 16-byte aligned and N % 4 == 0: float4 stores
-  int* err;       // device error word: 0 ok, nonzero = a bounded wait gave up
+  int* err;  // device error word: 0 ok, nonzero = a bounded wait gave up
 };
 
 constexpr int kTcBK = 32;  // k per stage: one 128-byte swizzle row of fp32
 constexpr int kTcBM = 128;
+constexpr int kTcThreads = 320;
 
 inline int64_t tc_padded_k(int64_t K) { return (K + kTcBK - 1) / kTcBK * kTcBK; }
 
@@ -193,10 +200,10 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
                : "memory");
 }
 
-__device__ __forceinline__ uint32_t tf32_rna(float v) {
+__device__ __forceinline__ float tf32_rna(float v) {
   uint32_t r;
   asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(v));
-  return r;
+  return __uint_as_float(r);
 }
 
 #define FTB_TMEM_LD32(taddr, r)                                                                              \
@@ -216,34 +223,41 @@ struct TcSmem {
   static constexpr int B_BYTES = BN * kTcBK * 4;
   static constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
   static constexpr int TX_BYTES = A_BYTES + 2 * B_BYTES;  // what TMA writes per stage
-  static constexpr int BAR_BYTES = 8 * (3 * STAGES + 2) + 16;
-  static constexpr int TOTAL = 1024 + STAGES * STAGE_BYTES + BAR_BYTES;
+  static constexpr int EPI_BYTES = 4 * 32 * 33 * 4;       // per epilogue warp: a 32 x 32 transpose tile
+  static constexpr int NBAR = 3 * STAGES + 5;
+  static constexpr int BAR_BYTES = 8 * NBAR + 16;
+  static constexpr int TOTAL = 1024 + STAGES * STAGE_BYTES + EPI_BYTES + BAR_BYTES;
 };
 
 template <int BN, int STAGES>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(kTcThreads, 1)
 tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_bhi,
                const __grid_constant__ CUtensorMap map_blo, TcKernelParams p) {
   using L = TcSmem<BN, STAGES>;
+  static_assert(L::TOTAL <= 227 * 1024, "shared memory budget");
+  static_assert(2 * BN <= 512, "two accumulators must fit in TMEM");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   auto a_tile = [&](int s) { return reinterpret_cast<float*>(smem + s * L::STAGE_BYTES); };
   auto alo_tile = [&](int s) { return reinterpret_cast<float*>(smem + s * L::STAGE_BYTES + L::A_BYTES); };
   auto bhi_tile = [&](int s) { return smem + s * L::STAGE_BYTES + 2 * L::A_BYTES; };
   auto blo_tile = [&](int s) { return smem + s * L::STAGE_BYTES + 2 * L::A_BYTES + L::B_BYTES; };
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * L::STAGE_BYTES);
-  uint64_t* full = bars;                 // TMA landed
-  uint64_t* conv = bars + STAGES;        // A split into hi / lo
-  uint64_t* empty = bars + 2 * STAGES;   // MMAs done reading the stage
-  uint64_t* accf = bars + 3 * STAGES;    // accumulator complete
-  uint64_t* drain = bars + 3 * STAGES + 1;
-  volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(bars + 3 * STAGES + 2);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 3 * STAGES + 2) + 1;
+  float* epi_stage = reinterpret_cast<float*>(smem + STAGES * L::STAGE_BYTES);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * L::STAGE_BYTES + L::EPI_BYTES);
+  uint64_t* full = bars;                // TMA landed
+  uint64_t* conv = bars + STAGES;       // A split into hi / lo
+  uint64_t* empty = bars + 2 * STAGES;  // MMAs done reading the stage
+  uint64_t* accf = bars + 3 * STAGES;   // [2] accumulator buffer complete
+  uint64_t* acce = accf + 2;            // [2] accumulator buffer drained by the epilogue
+  uint64_t* drain = acce + 2;           // MMAs retired after an abort
+  volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(drain + 1) + 1;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int m0 = blockIdx.x * kTcBM;
-  const int n0 = blockIdx.y * BN;
+  const int tiles_m = (p.M + kTcBM - 1) / kTcBM;
+  const int tiles_n = (p.N + BN - 1) / BN;
+  const int ntiles = tiles_m * tiles_n;
   const int nk = (p.K + kTcBK - 1) / kTcBK;
 
   if (threadIdx.x == 0) {
@@ -252,16 +266,18 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
       mbar_init(&conv[s], 4);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(accf, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&accf[b], 1);
+      mbar_init(&acce[b], 4);
+    }
     mbar_init(drain, 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {
-    // BN fp32 columns of TMEM for the 128 x BN accumulator
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_u32(const_cast<uint32_t*>(tmem_slot))),
-                 "r"((uint32_t)BN)
+                 "r"((uint32_t)(2 * BN))
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
@@ -273,109 +289,124 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
   if (warp == 0) {
     if (lane == 0) {
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_a)) : "memory");
-      for (int kb = 0; kb < nk; ++kb) {
-        const int s = kb % STAGES;
-        const uint32_t r = (uint32_t)(kb / STAGES);
-        if (!mbar_wait(&empty[s], (r & 1u) ^ 1u, abort_flag, p.err, 1)) break;
-        mbar_arrive_expect_tx(&full[s], L::TX_BYTES);
-        tma_load_2d(a_tile(s), &map_a, kb * kTcBK, m0, &full[s]);
-        tma_load_2d(bhi_tile(s), &map_bhi, kb * kTcBK, n0, &full[s]);
-        tma_load_2d(blo_tile(s), &map_blo, kb * kTcBK, n0, &full[s]);
+      uint32_t it = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+        const int m0 = (t / tiles_n) * kTcBM;
+        const int n0 = (t % tiles_n) * BN;
+        for (int kb = 0; kb < nk; ++kb, ++it) {
+          const int s = (int)(it % STAGES);
+          const uint32_t r = it / STAGES;
+          if (!(ok = mbar_wait(&empty[s], (r & 1u) ^ 1u, abort_flag, p.err, 1))) break;
+          mbar_arrive_expect_tx(&full[s], L::TX_BYTES);
+          tma_load_2d(a_tile(s), &map_a, kb * kTcBK, m0, &full[s]);
+          tma_load_2d(bhi_tile(s), &map_bhi, kb * kTcBK, n0, &full[s]);
+          tma_load_2d(blo_tile(s), &map_blo, kb * kTcBK, n0, &full[s]);
+        }
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
       const uint32_t idesc = idesc_tf32<BN>();
+      uint32_t it = 0, tc = 0;
       bool ok = true;
-      for (int kb = 0; kb < nk && ok; ++kb) {
-        const int s = kb % STAGES;
-        const uint32_t par = (uint32_t)(kb / STAGES) & 1u;
-        ok = mbar_wait(&full[s], par, abort_flag, p.err, 2) && mbar_wait(&conv[s], par, abort_flag, p.err, 3);
-        if (!ok) break;
+      for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x, ++tc) {
+        const uint32_t buf = tc & 1u, use = tc >> 1;
+        if (!(ok = mbar_wait(&acce[buf], (use & 1u) ^ 1u, abort_flag, p.err, 2))) break;
         tc_fence_after();
-        const uint32_t ahi = smem_u32(a_tile(s)), alo = smem_u32(alo_tile(s));
-        const uint32_t bhi = smem_u32(bhi_tile(s)), blo = smem_u32(blo_tile(s));
+        const uint32_t d = tmem + buf * (uint32_t)BN;
+        for (int kb = 0; kb < nk; ++kb, ++it) {
+          const int s = (int)(it % STAGES);
+          const uint32_t par = (it / STAGES) & 1u;
+          ok = mbar_wait(&full[s], par, abort_flag, p.err, 3) && mbar_wait(&conv[s], par, abort_flag, p.err, 4);
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t ahi = smem_u32(a_tile(s)), alo = smem_u32(alo_tile(s));
+          const uint32_t bhi = smem_u32(bhi_tile(s)), blo = smem_u32(blo_tile(s));
 #pragma unroll
-        for (int j = 0; j < kTcBK / 8; ++j) {  // K = 8 tf32 (32 bytes) per MMA
-          const uint32_t off = (uint32_t)j * 32u;
-          const uint64_t dah = smem_desc_sw128(ahi + off), dal = smem_desc_sw128(alo + off);
-          const uint64_t dbh = smem_desc_sw128(bhi + off), dbl = smem_desc_sw128(blo + off);
-          umma_tf32(tmem, dah, dbh, idesc, (kb > 0 || j > 0) ? 1u : 0u);
-          umma_tf32(tmem, dah, dbl, idesc, 1u);
-          umma_tf32(tmem, dal, dbh, idesc, 1u);
+          for (int j = 0; j < kTcBK / 8; ++j) {  // K = 8 tf32 (32 bytes) per MMA
+            const uint32_t off = (uint32_t)j * 32u;
+            const uint64_t dah = smem_desc_sw128(ahi + off), dal = smem_desc_sw128(alo + off);
+            const uint64_t dbh = smem_desc_sw128(bhi + off), dbl = smem_desc_sw128(blo + off);
+            umma_tf32(d, dah, dbh, idesc, (kb > 0 || j > 0) ? 1u : 0u);
+            umma_tf32(d, dah, dbl, idesc, 1u);
+            umma_tf32(d, dal, dbh, idesc, 1u);
+          }
+          umma_commit(&empty[s]);
         }
-        umma_commit(&empty[s]);
+        if (ok) umma_commit(&accf[buf]);
       }
-      // accumulator ready (or, after an abort, every issued MMA retired)
-      umma_commit(ok ? accf : drain);
-      if (!ok) mbar_wait(drain, 0, abort_flag, p.err, 4);
+      if (!ok) {
+        umma_commit(drain);  // every MMA issued so far retires before this arrives
+        mbar_wait(drain, 0, abort_flag, p.err, 5);
+      }
+    }
+  } else if (warp < 6) {
+    // warps 2..5: split A into tf32 hi (in place) and lo
+    const int t128 = threadIdx.x - 64;
+    uint32_t it = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+      for (int kb = 0; kb < nk; ++kb, ++it) {
+        const int s = (int)(it % STAGES);
+        if (!(ok = mbar_wait(&full[s], (it / STAGES) & 1u, abort_flag, p.err, 6))) break;
+        float4* hi = reinterpret_cast<float4*>(a_tile(s));
+        float4* lo = reinterpret_cast<float4*>(alo_tile(s));
+#pragma unroll
+        for (int i = 0; i < (kTcBM * kTcBK / 4) / 128; ++i) {
+          const int idx = t128 + i * 128;
+          const float4 v = hi[idx];
+          float4 h, l;
+          h.x = tf32_rna(v.x);
+          h.y = tf32_rna(v.y);
+          h.z = tf32_rna(v.z);
+          h.w = tf32_rna(v.w);
+          l.x = tf32_rna(v.x - h.x);
+          l.y = tf32_rna(v.y - h.y);
+          l.z = tf32_rna(v.z - h.z);
+          l.w = tf32_rna(v.w - h.w);
+          hi[idx] = h;
+          lo[idx] = l;
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&conv[s]);
+      }
     }
   } else {
-    // warps 2..5: split A, then the epilogue
-    const int t = threadIdx.x - 64;  // 0..127
-    bool ok = true;
-    for (int kb = 0; kb < nk && ok; ++kb) {
-      const int s = kb % STAGES;
-      const uint32_t par = (uint32_t)(kb / STAGES) & 1u;
-      ok = mbar_wait(&full[s], par, abort_flag, p.err, 5);
-      if (!ok) break;
-      float4* hi = reinterpret_cast<float4*>(a_tile(s));
-      float4* lo = reinterpret_cast<float4*>(alo_tile(s));
-#pragma unroll
-      for (int i = 0; i < (kTcBM * kTcBK / 4) / 128; ++i) {
-        const int idx = t + i * 128;
-        const float4 v = hi[idx];
-        float4 h, l;
-        h.x = __uint_as_float(tf32_rna(v.x));
-        h.y = __uint_as_float(tf32_rna(v.y));
-        h.z = __uint_as_float(tf32_rna(v.z));
-        h.w = __uint_as_float(tf32_rna(v.w));
-        l.x = v.x - h.x;
-        l.y = v.y - h.y;
-        l.z = v.z - h.z;
-        l.w = v.w - h.w;
-        hi[idx] = h;
-        lo[idx] = l;
-      }
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&conv[s]);
-    }
-    const bool have_acc = ok && mbar_wait(accf, 0, abort_flag, p.err, 6);
-    tc_fence_after();
-    __syncwarp();
-    if (have_acc) {
-      const int q = warp & 3;  // TMEM lane quarter this warp may access
-      const int row = q * 32 + lane;
-      const int m = m0 + row;
-      const uint32_t base = tmem + ((uint32_t)(q * 32) << 16);
+    // warps 6..9: epilogue, one TMEM lane quarter each
+    const int q = warp & 3;
+    float* tr = epi_stage + (warp - 6) * 32 * 33;
+    uint32_t tc = 0;
+    for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++tc) {
+      const uint32_t buf = tc & 1u, use = tc >> 1;
+      if (!mbar_wait(&accf[buf], use & 1u, abort_flag, p.err, 7)) break;
+      tc_fence_after();
+      const int m0 = (t / tiles_n) * kTcBM;
+      const int n0 = (t % tiles_n) * BN;
+      const uint32_t base = tmem + buf * (uint32_t)BN + ((uint32_t)(q * 32) << 16);
 #pragma unroll 1
       for (int c = 0; c < BN; c += 32) {
         uint32_t r[32];
         __syncwarp();  // tcgen05.ld is warp-collective
         FTB_TMEM_LD32(base + (uint32_t)c, r);
         asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-        if (m < p.M) {
-          const int nb = n0 + c;
-          float* yrow = p.Y + (int64_t)m * p.N;
-          if (nb + 32 <= p.N && p.vec_store) {
+        // lane holds row (q*32 + lane), columns c..c+31: transpose through smem
 #pragma unroll
-            for (int j = 0; j < 32; j += 4) {
-              float4 o;
-              o.x = apply_epilogue(__uint_as_float(r[j + 0]), p.epi, p.bias, p.res, m, nb + j + 0, p.N);
-              o.y = apply_epilogue(__uint_as_float(r[j + 1]), p.epi, p.bias, p.res, m, nb + j + 1, p.N);
-              o.z = apply_epilogue(__uint_as_float(r[j + 2]), p.epi, p.bias, p.res, m, nb + j + 2, p.N);
-              o.w = apply_epilogue(__uint_as_float(r[j + 3]), p.epi, p.bias, p.res, m, nb + j + 3, p.N);
-              *reinterpret_cast<float4*>(yrow + nb + j) = o;
-            }
-          } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (nb + j < p.N)
-                yrow[nb + j] = apply_epilogue(__uint_as_float(r[j]), p.epi, p.bias, p.res, m, nb + j, p.N);
+        for (int j = 0; j < 32; ++j) tr[lane * 33 + j] = __uint_as_float(r[j]);
+        __syncwarp();
+        const int n = n0 + c + lane;
+        if (n < p.N) {
+          const int rows = min(32, p.M - (m0 + q * 32));
+          for (int i = 0; i < rows; ++i) {
+            const int m = m0 + q * 32 + i;
+            p.Y[(int64_t)m * p.N + n] = apply_epilogue(tr[i * 33 + lane], p.epi, p.bias, p.res, m, n, p.N);
           }
         }
       }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acce[buf]);
     }
   }
   tc_fence_before();
@@ -383,7 +414,8 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)BN) : "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)(2 * BN))
+                 : "memory");
   }
 }
 
@@ -437,7 +469,7 @@ inline bool tc_prepare_weights(TcWeights& w, int64_t N) {
 // Returns 0 when launched, 1 when this GEMM cannot take the tensor-core path
 // (unaligned operand: the caller runs the SIMT kernel), -1 on a launch error.
 template <int BN, int STAGES>
-inline int launch_tc_bn(const TcArgs& t, const TcWeights& w, int* err, cudaStream_t s) {
+inline int launch_tc_bn(const TcArgs& t, const TcWeights& w, int* err, int sm_count, cudaStream_t s) {
   using L = TcSmem<BN, STAGES>;
   static bool attr_set = false;
   if (!attr_set) {
@@ -456,31 +488,30 @@ inline int launch_tc_bn(const TcArgs& t, const TcWeights& w, int* err, cudaStrea
   p.N = (int)t.N;
   p.K = (int)t.K;
   p.epi = t.epi;
-  p.vec_store = ((reinterpret_cast<uintptr_t>(t.Y) & 15) == 0 && (t.N & 3) == 0) ? 1 : 0;
   p.err = err;
   // the accumulator starts at zero: a bias-first epilogue adds the bias at the end
   if (p.epi & EPI_BIAS_FIRST) p.epi = (p.epi & ~(uint32_t)EPI_BIAS_FIRST) | EPI_BIAS_LAST;
-  dim3 grid((unsigned)((t.M + kTcBM - 1) / kTcBM), (unsigned)((t.N + BN - 1) / BN));
+  const int64_t ntiles = ((t.M + kTcBM - 1) / kTcBM) * ((t.N + BN - 1) / BN);
+  const unsigned grid = (unsigned)std::min<int64_t>(ntiles, sm_count);
   const int bi = tc_bn_index(BN);
-  tc_gemm_kernel<BN, STAGES><<<grid, 192, L::TOTAL, s>>>(map_a, w.map_hi[bi], w.map_lo[bi], p);
+  tc_gemm_kernel<BN, STAGES><<<grid, kTcThreads, L::TOTAL, s>>>(map_a, w.map_hi[bi], w.map_lo[bi], p);
   return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 
 inline int tc_choose_bn(int64_t M, int64_t N, int sm_count) {
+  (void)M;
+  (void)sm_count;
   if (N <= 64) return 64;
-  if (N <= 128) return 128;
-  // wide layers: 256-wide tiles when they still give two full waves
-  const int64_t tiles256 = ((M + kTcBM - 1) / kTcBM) * ((N + 255) / 256);
-  return tiles256 >= 2 * sm_count ? 256 : 128;
+  return 128;
 }
 
 inline int launch_tc_gemm(const TcArgs& t, const TcWeights& w, int* err, int sm_count, cudaStream_t s) {
   if (!w.maps_ready || t.M <= 0) return 1;
   if (t.M > 0x7fffffff / 2 || t.N > 65535 * 64) return 1;
   switch (tc_choose_bn(t.M, t.N, sm_count)) {
-    case 64: return launch_tc_bn<64, 4>(t, w, err, s);
-    case 128: return launch_tc_bn<128, 3>(t, w, err, s);
-    default: return launch_tc_bn<256, 2>(t, w, err, s);
+    case 64: return launch_tc_bn<64, 4>(t, w, err, sm_count, s);
+    case 128: return launch_tc_bn<128, 3>(t, w, err, sm_count, s);
+    default: return launch_tc_bn<256, 2>(t, w, err, sm_count, s);
   }
 }
 
