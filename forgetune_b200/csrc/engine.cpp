@@ -537,6 +537,20 @@ Program build_program(const void* blob, size_t bytes) {
     s.static_rows = !o.shape.dynamic();
     prog.steps.push_back(s);
   }
+  // small-N heads a tensor-core GEMM may compute in its epilogue
+  const auto uc = g.use_counts();
+  for (size_t i = 0; i + 1 < prog.steps.size(); ++i) {
+    Step& a = prog.steps[i];
+    Step& b = prog.steps[i + 1];
+    if (a.kind != ST_GEMM || b.kind != ST_GEMM || a.static_rows || b.static_rows) continue;
+    if (a.out.space != SP_ARENA || b.a.space != SP_ARENA || b.a.offset != a.out.offset) continue;
+    if (uc.at(static_cast<size_t>(a.node_id)) != 1) continue;
+    if (b.K != a.N || b.N > kMaxHeadN || a.N > kMaxHeadK) continue;
+    if (b.epi & (EPI_RESIDUAL | EPI_BIAS_ROWS)) continue;
+    if (b.bias.space != SP_NONE && b.bias.space != SP_WEIGHT) continue;
+    a.head_step = static_cast<int32_t>(i + 1);
+    b.head_of = static_cast<int32_t>(i);
+  }
   return prog;
 }
 

@@ -180,7 +180,15 @@ struct Step {
   // W^T split into tf32 hi / lo [N,Kp] for the tensor-core path
   uint64_t w_kn = 0, w_nk_hi = 0, w_nk_lo = 0;
   int64_t Kp = 0;  // K padded to the tensor-core k-block
+  // Small-N head: the GEMM step right after this one consumes only this
+  // step's output and has N <= kMaxHeadN, so a tensor-core launch of this
+  // step can compute it in its epilogue (the intermediate is never stored).
+  int32_t head_step = -1;  // index of that step, or -1
+  int32_t head_of = -1;    // on the head step: the step that may absorb it
 };
+
+constexpr int64_t kMaxHeadN = 16;
+constexpr int64_t kMaxHeadK = 256;
 
 struct Program {
   Graph graph;

@@ -459,10 +459,12 @@ static int enqueue(const Model* m, const Replica* rep, char* arena, const float*
     }
   };
   const int sm = rep->sm_count;
+  size_t skip_step = (size_t)-1;  // a head step already computed by the previous GEMM's epilogue
   for (size_t i = 0; i < rep->steps.size(); ++i) {
     const Step& st = rep->steps[i];
     const int64_t rows = st.static_rows ? 1 : batch;
     if (marks) cudaEventRecord(marks[i], s);
+    if (i == skip_step) continue;
     switch (st.kind) {
       case ST_GEMM:
       case ST_CONV: {
@@ -502,7 +504,22 @@ static int enqueue(const Model* m, const Replica* rep, char* arena, const float*
             t.K = st.K;
             t.Kp = tw.Kp;
             t.epi = st.epi;
+            if (st.head_step >= 0) {
+              const Step& hs = rep->steps[(size_t)st.head_step];
+              t.head.w = ptr(hs.b);
+              t.head.bias = hs.bias.space ? ptr(hs.bias) : nullptr;
+              t.head.y = ptr(hs.out);
+              t.head.n = (int)hs.N;
+              t.head.epi = hs.epi;
+            }
             tc_rc = launch_tc_gemm(t, tw, rep->err_dev, sm, s);
+            if (tc_rc == 1 && st.head_step >= 0) {
+              // the fused form does not apply: plain tensor-core GEMM, head runs as its own step
+              t.head = TcHead{};
+              tc_rc = launch_tc_gemm(t, tw, rep->err_dev, sm, s);
+            } else if (tc_rc == 0 && st.head_step >= 0) {
+              skip_step = (size_t)st.head_step;
+            }
             if (tc_rc < 0) {
               set_error(std::string("tensor-core GEMM launch failed: ") + cudaGetErrorString(cudaGetLastError()));
               return ST_DEVICE;

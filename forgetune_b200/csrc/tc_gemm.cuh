@@ -47,6 +47,16 @@ struct TcWeights {
   bool maps_ready = false;
 };
 
+// Small-N head computed in the epilogue: y2[m, :] = epi2(y[m, :] W2 + b2),
+// with y never stored (W2 is [N, head_n] row-major, head_n <= 16).
+struct TcHead {
+  const float* w = nullptr;
+  const float* bias = nullptr;
+  float* y = nullptr;
+  int n = 0;
+  uint32_t epi = 0;
+};
+
 struct TcArgs {
   const float* A;
   const float* w_hi;
@@ -56,6 +66,7 @@ struct TcArgs {
   float* Y;
   int64_t M, N, K, Kp;
   uint32_t epi;
+  TcHead head;
 };
 
 struct TcKernelParams {
@@ -64,8 +75,12 @@ struct TcKernelParams {
   float* Y;
   int M, N, K;
   uint32_t epi;
+  TcHead head;
   int* err;  // device error word: 0 ok, nonzero = a bounded wait gave up
 };
+
+constexpr int kTcMaxHeadN = 16;
+constexpr int kTcMaxHeadK = 256;
 
 constexpr int kTcBK = 32;  // k per stage: one 128-byte swizzle row of fp32
 constexpr int kTcBM = 128;
@@ -224,9 +239,10 @@ struct TcSmem {
   static constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
   static constexpr int TX_BYTES = A_BYTES + 2 * B_BYTES;  // what TMA writes per stage
   static constexpr int EPI_BYTES = 4 * 32 * 33 * 4;       // per epilogue warp: a 32 x 32 transpose tile
+  static constexpr int HEAD_BYTES = (kTcMaxHeadK + 1) * kTcMaxHeadN * 4;  // head weights + bias
   static constexpr int NBAR = 3 * STAGES + 5;
   static constexpr int BAR_BYTES = 8 * NBAR + 16;
-  static constexpr int TOTAL = 1024 + STAGES * STAGE_BYTES + EPI_BYTES + BAR_BYTES;
+  static constexpr int TOTAL = 1024 + STAGES * STAGE_BYTES + EPI_BYTES + HEAD_BYTES + BAR_BYTES;
 };
 
 template <int BN, int STAGES>
@@ -243,7 +259,8 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
   auto bhi_tile = [&](int s) { return smem + s * L::STAGE_BYTES + 2 * L::A_BYTES; };
   auto blo_tile = [&](int s) { return smem + s * L::STAGE_BYTES + 2 * L::A_BYTES + L::B_BYTES; };
   float* epi_stage = reinterpret_cast<float*>(smem + STAGES * L::STAGE_BYTES);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * L::STAGE_BYTES + L::EPI_BYTES);
+  float* head_smem = reinterpret_cast<float*>(smem + STAGES * L::STAGE_BYTES + L::EPI_BYTES);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * L::STAGE_BYTES + L::EPI_BYTES + L::HEAD_BYTES);
   uint64_t* full = bars;                // TMA landed
   uint64_t* conv = bars + STAGES;       // A split into hi / lo
   uint64_t* empty = bars + 2 * STAGES;  // MMAs done reading the stage
@@ -377,6 +394,14 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
     // warps 6..9: epilogue, one TMEM lane quarter each
     const int q = warp & 3;
     float* tr = epi_stage + (warp - 6) * 32 * 33;
+    const int hn = p.head.n;
+    if (hn > 0) {
+      // head weights [N, hn] then bias [hn], shared by the four epilogue warps
+      for (int i = threadIdx.x - 192; i < p.N * hn; i += 128) head_smem[i] = p.head.w[i];
+      for (int i = threadIdx.x - 192; i < hn; i += 128)
+        head_smem[p.N * hn + i] = p.head.bias ? p.head.bias[i] : 0.0f;
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+    }
     uint32_t tc = 0;
     for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++tc) {
       const uint32_t buf = tc & 1u, use = tc >> 1;
@@ -385,6 +410,43 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
       const int m0 = (t / tiles_n) * kTcBM;
       const int n0 = (t % tiles_n) * BN;
       const uint32_t base = tmem + buf * (uint32_t)BN + ((uint32_t)(q * 32) << 16);
+      if (hn > 0) {
+        // the tile holds whole rows (N <= BN): lane = row, accumulate the head
+        const int m = m0 + q * 32 + lane;
+        float acc[kTcMaxHeadN];
+#pragma unroll
+        for (int o = 0; o < kTcMaxHeadN; ++o) acc[o] = 0.0f;
+#pragma unroll 1
+        for (int c = 0; c < p.N; c += 32) {
+          uint32_t r[32];
+          __syncwarp();
+          FTB_TMEM_LD32(base + (uint32_t)c, r);
+          asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+          if (m < p.M) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              if (c + j < p.N) {
+                const float v = apply_epilogue(__uint_as_float(r[j]), p.epi, p.bias, p.res, m, c + j, p.N);
+                const float* wr = head_smem + (c + j) * hn;
+#pragma unroll
+                for (int o = 0; o < kTcMaxHeadN; ++o)
+                  if (o < hn) acc[o] = fmaf(v, wr[o], acc[o]);
+              }
+            }
+          }
+        }
+        if (m < p.M) {
+#pragma unroll
+          for (int o = 0; o < kTcMaxHeadN; ++o)
+            if (o < hn)
+              p.head.y[(int64_t)m * hn + o] =
+                  apply_epilogue(acc[o], p.head.epi, head_smem + p.N * hn, nullptr, m, o, hn);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acce[buf]);
+        continue;
+      }
 #pragma unroll 1
       for (int c = 0; c < BN; c += 32) {
         uint32_t r[32];
@@ -488,9 +550,12 @@ inline int launch_tc_bn(const TcArgs& t, const TcWeights& w, int* err, int sm_co
   p.N = (int)t.N;
   p.K = (int)t.K;
   p.epi = t.epi;
+  p.head = t.head;
   p.err = err;
   // the accumulator starts at zero: a bias-first epilogue adds the bias at the end
   if (p.epi & EPI_BIAS_FIRST) p.epi = (p.epi & ~(uint32_t)EPI_BIAS_FIRST) | EPI_BIAS_LAST;
+  if (p.head.epi & EPI_BIAS_FIRST) p.head.epi = (p.head.epi & ~(uint32_t)EPI_BIAS_FIRST) | EPI_BIAS_LAST;
+  if (p.head.n > 0 && (t.N > BN || p.head.n > kTcMaxHeadN || t.N > kTcMaxHeadK)) return 1;
   const int64_t ntiles = ((t.M + kTcBM - 1) / kTcBM) * ((t.N + BN - 1) / BN);
   const unsigned grid = (unsigned)std::min<int64_t>(ntiles, sm_count);
   const int bi = tc_bn_index(BN);
@@ -498,17 +563,20 @@ inline int launch_tc_bn(const TcArgs& t, const TcWeights& w, int* err, int sm_co
   return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 
-inline int tc_choose_bn(int64_t M, int64_t N, int sm_count) {
+inline int tc_choose_bn(int64_t M, int64_t N, int sm_count, bool head) {
   (void)M;
   (void)sm_count;
   if (N <= 64) return 64;
-  return 128;
+  if (N <= 128) return 128;
+  // a fused head needs whole rows in one tile; otherwise 256-wide tiles
+  // halve the re-reads of A for layers whose width is a multiple of 256
+  return (head || N % 256 == 0) ? 256 : 128;
 }
 
 inline int launch_tc_gemm(const TcArgs& t, const TcWeights& w, int* err, int sm_count, cudaStream_t s) {
   if (!w.maps_ready || t.M <= 0) return 1;
   if (t.M > 0x7fffffff / 2 || t.N > 65535 * 64) return 1;
-  switch (tc_choose_bn(t.M, t.N, sm_count)) {
+  switch (tc_choose_bn(t.M, t.N, sm_count, t.head.n > 0)) {
     case 64: return launch_tc_bn<64, 4>(t, w, err, sm_count, s);
     case 128: return launch_tc_bn<128, 3>(t, w, err, sm_count, s);
     default: return launch_tc_bn<256, 2>(t, w, err, sm_count, s);

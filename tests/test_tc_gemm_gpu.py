@@ -63,3 +63,23 @@ def test_tcgen05_matches_oracle(M, K, N, relu, residual, tmp_path):
     again = cm.run(x)
     assert np.array_equal(got.view(np.uint32), again.view(np.uint32))
     cm.close()
+
+
+@pytest.mark.parametrize("M,K,H,N2", [(3000, 96, 128, 7), (65536, 256, 128, 10), (1500, 64, 256, 16),
+                                      (2000, 128, 200, 3), (1024, 128, 320, 10)])
+def test_fused_small_head_matches_oracle(M, K, H, N2, tmp_path):
+    """Linear+ReLU followed by a Linear with <= 16 outputs: the head is
+    computed in the tensor-core epilogue (the hidden layer is never stored)
+    when the hidden width fits one tile, and as its own step otherwise."""
+    torch.manual_seed(M + H)
+    m = nn.Sequential(nn.Linear(K, H), nn.ReLU(), nn.Linear(H, N2)).eval()
+    cm = compile_model(m, (torch.randn(2, K),), output_dir=str(tmp_path), autotune=False, enable_fusion=True,
+                       kernel_variant="fused_ikj", dynamic_batch=True, max_batch_size=M,
+                       max_workspace_bytes=8 << 30, gpu_kernel="tcgen05", verify=False)
+    x = np.random.default_rng(H).standard_normal((M, K)).astype(np.float32)
+    got = cm.run(x)
+    want = oracle.run_model(m, x, "naive_ijk")
+    assert got.shape == (M, N2)
+    assert np.allclose(got, want, atol=1e-4, rtol=1e-4), float(np.max(np.abs(got - want)))
+    assert np.array_equal(got.view(np.uint32), cm.run(x).view(np.uint32))
+    cm.close()
