@@ -239,7 +239,8 @@ struct TcSmem {
   static constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
   static constexpr int TX_BYTES = A_BYTES + 2 * B_BYTES;  // what TMA writes per stage
   static constexpr int EPI_BYTES = 4 * 32 * 33 * 4;       // per epilogue warp: a 32 x 32 transpose tile
-  static constexpr int HEAD_BYTES = (kTcMaxHeadK + 1) * kTcMaxHeadN * 4;  // head weights + bias
+  // head weights [256][16], this GEMM's bias [256], the head's bias [16]
+  static constexpr int HEAD_BYTES = (kTcMaxHeadK * kTcMaxHeadN + kTcMaxHeadK + kTcMaxHeadN) * 4;
   static constexpr int NBAR = 3 * STAGES + 5;
   static constexpr int BAR_BYTES = 8 * NBAR + 16;
   static constexpr int TOTAL = 1024 + STAGES * STAGE_BYTES + EPI_BYTES + HEAD_BYTES + BAR_BYTES;
@@ -395,11 +396,20 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
     const int q = warp & 3;
     float* tr = epi_stage + (warp - 6) * 32 * 33;
     const int hn = p.head.n;
+    const int hp = (hn + 3) & ~3;  // head width padded to whole float4s
+    float* head_w = head_smem;                       // [N][hp], zero padded
+    float* head_ba = head_smem + kTcMaxHeadK * kTcMaxHeadN;  // bias of this GEMM, [N]
+    float* head_bb = head_ba + kTcMaxHeadK;                  // bias of the head, [hp]
+    const float* bias_a = (p.epi & EPI_BIAS_ROWS) ? p.bias : head_ba;
     if (hn > 0) {
-      // head weights [N, hn] then bias [hn], shared by the four epilogue warps
-      for (int i = threadIdx.x - 192; i < p.N * hn; i += 128) head_smem[i] = p.head.w[i];
-      for (int i = threadIdx.x - 192; i < hn; i += 128)
-        head_smem[p.N * hn + i] = p.head.bias ? p.head.bias[i] : 0.0f;
+      // stage the head weights and both biases once; all four epilogue warps read them
+      for (int i = threadIdx.x - 192; i < p.N * hp; i += 128) {
+        const int k = i / hp, o = i - k * hp;
+        head_w[i] = o < hn ? p.head.w[k * hn + o] : 0.0f;
+      }
+      for (int i = threadIdx.x - 192; i < p.N; i += 128)
+        head_ba[i] = (p.bias && !(p.epi & EPI_BIAS_ROWS)) ? p.bias[i] : 0.0f;
+      for (int i = threadIdx.x - 192; i < hp; i += 128) head_bb[i] = (p.head.bias && i < hn) ? p.head.bias[i] : 0.0f;
       asm volatile("bar.sync 1, 128;" ::: "memory");
     }
     uint32_t tc = 0;
@@ -425,12 +435,19 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
           if (m < p.M) {
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
-              if (c + j < p.N) {
-                const float v = apply_epilogue(__uint_as_float(r[j]), p.epi, p.bias, p.res, m, c + j, p.N);
-                const float* wr = head_smem + (c + j) * hn;
+              if (c + j < p.N) {  // warp-uniform
+                const float v = apply_epilogue(__uint_as_float(r[j]), p.epi, bias_a, p.res, m, c + j, p.N);
+                const float4* w4 = reinterpret_cast<const float4*>(head_w + (c + j) * hp);
 #pragma unroll
-                for (int o = 0; o < kTcMaxHeadN; ++o)
-                  if (o < hn) acc[o] = fmaf(v, wr[o], acc[o]);
+                for (int o4 = 0; o4 < kTcMaxHeadN / 4; ++o4) {
+                  if (o4 * 4 < hn) {  // warp-uniform
+                    const float4 w = w4[o4];
+                    acc[4 * o4 + 0] = fmaf(v, w.x, acc[4 * o4 + 0]);
+                    acc[4 * o4 + 1] = fmaf(v, w.y, acc[4 * o4 + 1]);
+                    acc[4 * o4 + 2] = fmaf(v, w.z, acc[4 * o4 + 2]);
+                    acc[4 * o4 + 3] = fmaf(v, w.w, acc[4 * o4 + 3]);
+                  }
+                }
               }
             }
           }
@@ -439,8 +456,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
 #pragma unroll
           for (int o = 0; o < kTcMaxHeadN; ++o)
             if (o < hn)
-              p.head.y[(int64_t)m * hn + o] =
-                  apply_epilogue(acc[o], p.head.epi, head_smem + p.N * hn, nullptr, m, o, hn);
+              p.head.y[(int64_t)m * hn + o] = apply_epilogue(acc[o], p.head.epi, head_bb, nullptr, m, o, hn);
         }
         tc_fence_before();
         __syncwarp();
