@@ -42,8 +42,8 @@ struct TcWeights {
   const float* hi = nullptr;  // W^T [N, Kp], tf32-rounded
   const float* lo = nullptr;  // tf32(W^T - hi)
   int64_t Kp = 0;
-  CUtensorMap map_hi[3];      // one per supported BN (64, 128, 256)
-  CUtensorMap map_lo[3];
+  CUtensorMap map_hi[2][3];   // [k-block 32 / 16][tile width 64 / 128 / 256]
+  CUtensorMap map_lo[2][3];
   bool maps_ready = false;
 };
 
@@ -82,7 +82,7 @@ struct TcKernelParams {
 constexpr int kTcMaxHeadN = 16;
 constexpr int kTcMaxHeadK = 256;
 
-constexpr int kTcBK = 32;  // k per stage: one 128-byte swizzle row of fp32
+constexpr int kTcBK = 32;  // k padding unit: one 128-byte swizzle row of fp32
 constexpr int kTcBM = 128;
 constexpr int kTcThreads = 320;
 
@@ -181,17 +181,19 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 
-// K-major operand tile in the 128-byte swizzle layout TMA wrote: rows of 128 B,
-// 8-row groups 1024 B apart.  Start address, leading byte offset 16 B
-// (unused by this layout), stride byte offset 1024 B, descriptor version 1,
-// layout type 2 (SWIZZLE_128B).
-__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr) {
+// K-major operand tile in the swizzle layout TMA wrote: rows of BK*4 bytes
+// (128 B for BK=32, 64 B for BK=16), 8-row groups 8*BK*4 bytes apart.  Start
+// address, leading byte offset 16 B (unused by these layouts), stride byte
+// offset, descriptor version 1, layout type 2 (SWIZZLE_128B) or 4 (SWIZZLE_64B).
+template <int BK>
+__device__ __forceinline__ uint64_t smem_desc_sw(uint32_t saddr) {
+  static_assert(BK == 32 || BK == 16, "k-block of 32 or 16 fp32");
   uint64_t d = 0;
   d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
   d |= (uint64_t)(16u >> 4) << 16;
-  d |= (uint64_t)(1024u >> 4) << 32;
+  d |= (uint64_t)((8u * BK * 4u) >> 4) << 32;
   d |= (uint64_t)1 << 46;
-  d |= (uint64_t)2 << 61;
+  d |= (uint64_t)(BK == 32 ? 2 : 4) << 61;
   return d;
 }
 
@@ -232,10 +234,10 @@ __device__ __forceinline__ float tf32_rna(float v) {
         "=r"(r[30]), "=r"(r[31])                                                                             \
       : "r"(taddr))
 
-template <int BN, int STAGES>
+template <int BN, int BK, int STAGES>
 struct TcSmem {
-  static constexpr int A_BYTES = kTcBM * kTcBK * 4;  // 16 KB
-  static constexpr int B_BYTES = BN * kTcBK * 4;
+  static constexpr int A_BYTES = kTcBM * BK * 4;
+  static constexpr int B_BYTES = BN * BK * 4;
   static constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
   static constexpr int TX_BYTES = A_BYTES + 2 * B_BYTES;  // what TMA writes per stage
   static constexpr int EPI_BYTES = 4 * 32 * 33 * 4;       // per epilogue warp: a 32 x 32 transpose tile
@@ -246,11 +248,11 @@ struct TcSmem {
   static constexpr int TOTAL = 1024 + STAGES * STAGE_BYTES + EPI_BYTES + HEAD_BYTES + BAR_BYTES;
 };
 
-template <int BN, int STAGES>
+template <int BN, int BK, int STAGES>
 __global__ void __launch_bounds__(kTcThreads, 1)
 tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_bhi,
                const __grid_constant__ CUtensorMap map_blo, TcKernelParams p) {
-  using L = TcSmem<BN, STAGES>;
+  using L = TcSmem<BN, BK, STAGES>;
   static_assert(L::TOTAL <= 227 * 1024, "shared memory budget");
   static_assert(2 * BN <= 512, "two accumulators must fit in TMEM");
   extern __shared__ uint8_t smem_raw[];
@@ -276,7 +278,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
   const int tiles_m = (p.M + kTcBM - 1) / kTcBM;
   const int tiles_n = (p.N + BN - 1) / BN;
   const int ntiles = tiles_m * tiles_n;
-  const int nk = (p.K + kTcBK - 1) / kTcBK;
+  const int nk = (p.K + BK - 1) / BK;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -317,9 +319,9 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
           const uint32_t r = it / STAGES;
           if (!(ok = mbar_wait(&empty[s], (r & 1u) ^ 1u, abort_flag, p.err, 1))) break;
           mbar_arrive_expect_tx(&full[s], L::TX_BYTES);
-          tma_load_2d(a_tile(s), &map_a, kb * kTcBK, m0, &full[s]);
-          tma_load_2d(bhi_tile(s), &map_bhi, kb * kTcBK, n0, &full[s]);
-          tma_load_2d(blo_tile(s), &map_blo, kb * kTcBK, n0, &full[s]);
+          tma_load_2d(a_tile(s), &map_a, kb * BK, m0, &full[s]);
+          tma_load_2d(bhi_tile(s), &map_bhi, kb * BK, n0, &full[s]);
+          tma_load_2d(blo_tile(s), &map_blo, kb * BK, n0, &full[s]);
         }
       }
     }
@@ -342,10 +344,10 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
           const uint32_t ahi = smem_u32(a_tile(s)), alo = smem_u32(alo_tile(s));
           const uint32_t bhi = smem_u32(bhi_tile(s)), blo = smem_u32(blo_tile(s));
 #pragma unroll
-          for (int j = 0; j < kTcBK / 8; ++j) {  // K = 8 tf32 (32 bytes) per MMA
+          for (int j = 0; j < BK / 8; ++j) {  // K = 8 tf32 (32 bytes) per MMA
             const uint32_t off = (uint32_t)j * 32u;
-            const uint64_t dah = smem_desc_sw128(ahi + off), dal = smem_desc_sw128(alo + off);
-            const uint64_t dbh = smem_desc_sw128(bhi + off), dbl = smem_desc_sw128(blo + off);
+            const uint64_t dah = smem_desc_sw<BK>(ahi + off), dal = smem_desc_sw<BK>(alo + off);
+            const uint64_t dbh = smem_desc_sw<BK>(bhi + off), dbl = smem_desc_sw<BK>(blo + off);
             umma_tf32(d, dah, dbh, idesc, (kb > 0 || j > 0) ? 1u : 0u);
             umma_tf32(d, dah, dbl, idesc, 1u);
             umma_tf32(d, dal, dbh, idesc, 1u);
@@ -371,7 +373,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
         float4* hi = reinterpret_cast<float4*>(a_tile(s));
         float4* lo = reinterpret_cast<float4*>(alo_tile(s));
 #pragma unroll
-        for (int i = 0; i < (kTcBM * kTcBK / 4) / 128; ++i) {
+        for (int i = 0; i < (kTcBM * BK / 4) / 128; ++i) {
           const int idx = t128 + i * 128;
           const float4 v = hi[idx];
           float4 h, l;
@@ -517,18 +519,19 @@ inline PFN_encodeTiled tma_encoder() {
 }
 
 // 2-D fp32 tensor map over a row-major [rows, cols] matrix with row stride
-// `ld` floats, box = [box_rows, 32] columns, 128-byte swizzle, zero fill.
-inline bool make_map_2d(CUtensorMap* map, const float* base, int64_t rows, int64_t cols, int64_t ld, int box_rows) {
+// `ld` floats, box = [box_rows, bk] columns, bk*4-byte swizzle, zero fill.
+inline bool make_map_2d(CUtensorMap* map, const float* base, int64_t rows, int64_t cols, int64_t ld, int box_rows,
+                        int bk) {
   PFN_encodeTiled enc = tma_encoder();
   if (!enc) return false;
   if ((reinterpret_cast<uintptr_t>(base) & 15) || (ld * 4) % 16) return false;
   cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)(ld * 4)};
-  cuuint32_t box[2] = {(cuuint32_t)kTcBK, (cuuint32_t)box_rows};
+  cuuint32_t box[2] = {(cuuint32_t)bk, (cuuint32_t)box_rows};
   cuuint32_t estr[2] = {1, 1};
   return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box, estr,
-             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+             CU_TENSOR_MAP_INTERLEAVE_NONE, bk == 32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 inline int tc_bn_index(int bn) { return bn == 64 ? 0 : bn == 128 ? 1 : 2; }
@@ -536,28 +539,30 @@ inline int tc_bn_index(int bn) { return bn == 64 ? 0 : bn == 128 ? 1 : 2; }
 // Weight maps for every tile width (built once per replica).
 inline bool tc_prepare_weights(TcWeights& w, int64_t N) {
   const int bns[3] = {64, 128, 256};
-  for (int i = 0; i < 3; ++i) {
-    if (!make_map_2d(&w.map_hi[i], w.hi, N, w.Kp, w.Kp, bns[i])) return false;
-    if (!make_map_2d(&w.map_lo[i], w.lo, N, w.Kp, w.Kp, bns[i])) return false;
-  }
+  const int bks[2] = {32, 16};
+  for (int b = 0; b < 2; ++b)
+    for (int i = 0; i < 3; ++i) {
+      if (!make_map_2d(&w.map_hi[b][i], w.hi, N, w.Kp, w.Kp, bns[i], bks[b])) return false;
+      if (!make_map_2d(&w.map_lo[b][i], w.lo, N, w.Kp, w.Kp, bns[i], bks[b])) return false;
+    }
   w.maps_ready = true;
   return true;
 }
 
 // Returns 0 when launched, 1 when this GEMM cannot take the tensor-core path
 // (unaligned operand: the caller runs the SIMT kernel), -1 on a launch error.
-template <int BN, int STAGES>
+template <int BN, int BK, int STAGES>
 inline int launch_tc_bn(const TcArgs& t, const TcWeights& w, int* err, int sm_count, cudaStream_t s) {
-  using L = TcSmem<BN, STAGES>;
+  using L = TcSmem<BN, BK, STAGES>;
   static bool attr_set = false;
   if (!attr_set) {
-    if (cudaFuncSetAttribute(tc_gemm_kernel<BN, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL) !=
-        cudaSuccess)
+    if (cudaFuncSetAttribute(tc_gemm_kernel<BN, BK, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             L::TOTAL) != cudaSuccess)
       return -1;
     attr_set = true;
   }
   CUtensorMap map_a;
-  if (!make_map_2d(&map_a, t.A, t.M, t.K, t.K, kTcBM)) return 1;
+  if (!make_map_2d(&map_a, t.A, t.M, t.K, t.K, kTcBM, BK)) return 1;
   TcKernelParams p;
   p.bias = t.bias;
   p.res = t.res;
@@ -575,7 +580,8 @@ inline int launch_tc_bn(const TcArgs& t, const TcWeights& w, int* err, int sm_co
   const int64_t ntiles = ((t.M + kTcBM - 1) / kTcBM) * ((t.N + BN - 1) / BN);
   const unsigned grid = (unsigned)std::min<int64_t>(ntiles, sm_count);
   const int bi = tc_bn_index(BN);
-  tc_gemm_kernel<BN, STAGES><<<grid, kTcThreads, L::TOTAL, s>>>(map_a, w.map_hi[bi], w.map_lo[bi], p);
+  const int ki = BK == 32 ? 0 : 1;
+  tc_gemm_kernel<BN, BK, STAGES><<<grid, kTcThreads, L::TOTAL, s>>>(map_a, w.map_hi[ki][bi], w.map_lo[ki][bi], p);
   return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 
@@ -592,10 +598,11 @@ inline int tc_choose_bn(int64_t M, int64_t N, int sm_count, bool head) {
 inline int launch_tc_gemm(const TcArgs& t, const TcWeights& w, int* err, int sm_count, cudaStream_t s) {
   if (!w.maps_ready || t.M <= 0) return 1;
   if (t.M > 0x7fffffff / 2 || t.N > 65535 * 64) return 1;
+  // k-blocks of 16 (64-byte swizzle) give twice the pipeline stages of 32
   switch (tc_choose_bn(t.M, t.N, sm_count, t.head.n > 0)) {
-    case 64: return launch_tc_bn<64, 4>(t, w, err, sm_count, s);
-    case 128: return launch_tc_bn<128, 3>(t, w, err, sm_count, s);
-    default: return launch_tc_bn<256, 2>(t, w, err, sm_count, s);
+    case 64: return launch_tc_bn<64, 16, 8>(t, w, err, sm_count, s);
+    case 128: return launch_tc_bn<128, 16, 6>(t, w, err, sm_count, s);
+    default: return launch_tc_bn<256, 16, 4>(t, w, err, sm_count, s);
   }
 }
 
