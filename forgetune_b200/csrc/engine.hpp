@@ -185,6 +185,11 @@ struct Step {
   // step can compute it in its epilogue (the intermediate is never stored).
   int32_t head_step = -1;  // index of that step, or -1
   int32_t head_of = -1;    // on the head step: the step that may absorb it
+  // tensor-core tile configuration chosen for this step (0 = by shape), and
+  // whether a head may be fused (set by the autotuner or the caller)
+  int32_t tc_bn = 0;
+  int32_t tc_bk = 0;
+  bool fuse_head = true;
 };
 
 constexpr int64_t kMaxHeadN = 16;

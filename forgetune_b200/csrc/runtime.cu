@@ -504,7 +504,10 @@ static int enqueue(const Model* m, const Replica* rep, char* arena, const float*
             t.K = st.K;
             t.Kp = tw.Kp;
             t.epi = st.epi;
-            if (st.head_step >= 0) {
+            TcConfig cfg;
+            cfg.bn = st.tc_bn;
+            cfg.bk = st.tc_bk;
+            if (st.head_step >= 0 && st.fuse_head) {
               const Step& hs = rep->steps[(size_t)st.head_step];
               t.head.w = ptr(hs.b);
               t.head.bias = hs.bias.space ? ptr(hs.bias) : nullptr;
@@ -512,12 +515,12 @@ static int enqueue(const Model* m, const Replica* rep, char* arena, const float*
               t.head.n = (int)hs.N;
               t.head.epi = hs.epi;
             }
-            tc_rc = launch_tc_gemm(t, tw, rep->err_dev, sm, s);
-            if (tc_rc == 1 && st.head_step >= 0) {
+            tc_rc = launch_tc_gemm(t, tw, rep->err_dev, sm, s, cfg);
+            if (tc_rc == 1 && t.head.n > 0) {
               // the fused form does not apply: plain tensor-core GEMM, head runs as its own step
               t.head = TcHead{};
-              tc_rc = launch_tc_gemm(t, tw, rep->err_dev, sm, s);
-            } else if (tc_rc == 0 && st.head_step >= 0) {
+              tc_rc = launch_tc_gemm(t, tw, rep->err_dev, sm, s, cfg);
+            } else if (tc_rc == 0 && t.head.n > 0) {
               skip_step = (size_t)st.head_step;
             }
             if (tc_rc < 0) {
@@ -860,6 +863,35 @@ FTB_API int ftb_model_set_policy(void* handle, int policy) {
   if (policy < KP_AUTO || policy > KP_TCGEN05) return ST_CONFIG;
   std::lock_guard<std::mutex> lk(m->mu);
   m->prog.graph.kernel_policy = policy;
+  for (ExecCtx* c : m->all_ctxs) {
+    for (auto& cg : c->graphs) cudaGraphExecDestroy(cg.exec);
+    c->graphs.clear();
+  }
+  return ST_OK;
+}
+
+// Tensor-core tile configuration of one launch-list step (0 = by shape) and
+// whether a following small-N head is fused into its epilogue.  Used by the
+// autotuner; call between runs, not concurrently with them.
+FTB_API int ftb_model_set_step_config(void* handle, int step, int tc_bn, int tc_bk, int fuse_head) {
+  auto* m = static_cast<Model*>(handle);
+  if (!m) return ST_NULL;
+  if (step < 0 || step >= (int)m->prog.steps.size()) {
+    set_error("step index out of range");
+    return ST_CONFIG;
+  }
+  if (!(tc_bn == 0 || tc_bn == 64 || tc_bn == 128 || tc_bn == 256) || !(tc_bk == 0 || tc_bk == 16 || tc_bk == 32)) {
+    set_error("tile width must be 0, 64, 128 or 256 and k-block 0, 16 or 32");
+    return ST_CONFIG;
+  }
+  std::lock_guard<std::mutex> lk(m->mu);
+  auto apply = [&](Step& s) {
+    s.tc_bn = tc_bn;
+    s.tc_bk = tc_bk;
+    s.fuse_head = fuse_head != 0;
+  };
+  apply(m->prog.steps[(size_t)step]);
+  for (auto& rep : m->replicas) apply(rep->steps[(size_t)step]);
   for (ExecCtx* c : m->all_ctxs) {
     for (auto& cg : c->graphs) cudaGraphExecDestroy(cg.exec);
     c->graphs.clear();

@@ -595,11 +595,28 @@ inline int tc_choose_bn(int64_t M, int64_t N, int sm_count, bool head) {
   return (head || N % 256 == 0) ? 256 : 128;
 }
 
-inline int launch_tc_gemm(const TcArgs& t, const TcWeights& w, int* err, int sm_count, cudaStream_t s) {
+// Tile configuration of one tensor-core launch: tile width BN and k-block BK.
+// 0 picks by shape.  Stages fill the shared memory: k-blocks of 16 (64-byte
+// swizzle) give twice the stages of 32.
+struct TcConfig {
+  int bn = 0;  // 64, 128 or 256
+  int bk = 0;  // 16 or 32
+};
+
+inline int launch_tc_gemm(const TcArgs& t, const TcWeights& w, int* err, int sm_count, cudaStream_t s,
+                          TcConfig cfg = TcConfig{}) {
   if (!w.maps_ready || t.M <= 0) return 1;
   if (t.M > 0x7fffffff / 2 || t.N > 65535 * 64) return 1;
-  // k-blocks of 16 (64-byte swizzle) give twice the pipeline stages of 32
-  switch (tc_choose_bn(t.M, t.N, sm_count, t.head.n > 0)) {
+  const int bn = cfg.bn ? cfg.bn : tc_choose_bn(t.M, t.N, sm_count, t.head.n > 0);
+  const int bk = cfg.bk ? cfg.bk : 16;
+  if (bk == 32) {
+    switch (bn) {
+      case 64: return launch_tc_bn<64, 32, 4>(t, w, err, sm_count, s);
+      case 128: return launch_tc_bn<128, 32, 3>(t, w, err, sm_count, s);
+      default: return launch_tc_bn<256, 32, 2>(t, w, err, sm_count, s);
+    }
+  }
+  switch (bn) {
     case 64: return launch_tc_bn<64, 16, 8>(t, w, err, sm_count, s);
     case 128: return launch_tc_bn<128, 16, 6>(t, w, err, sm_count, s);
     default: return launch_tc_bn<256, 16, 4>(t, w, err, sm_count, s);

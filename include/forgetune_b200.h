@@ -121,6 +121,10 @@ FORGETUNE_EXPORT int ftb_model_create(const void* blob, size_t bytes, void** mod
 FORGETUNE_EXPORT void ftb_model_destroy(void* model);
 FORGETUNE_EXPORT int ftb_model_set_devices(void* model, const int* device_ids, int n);
 FORGETUNE_EXPORT int ftb_model_set_policy(void* model, int policy);
+/* Tensor-core tile width (0, 64, 128, 256; 0 = by shape) and k-block (0, 16,
+ * 32) of launch-list step `step`, and whether a following small-N head is
+ * fused into its epilogue.  For the autotuner; call between runs. */
+FORGETUNE_EXPORT int ftb_model_set_step_config(void* model, int step, int tc_bn, int tc_bk, int fuse_head);
 FORGETUNE_EXPORT int ftb_model_prepare(void* model);
 FORGETUNE_EXPORT int ftb_model_run(void* model, const float* input, size_t input_count, float* output,
                                    size_t output_count, int64_t batch_size, int api);
