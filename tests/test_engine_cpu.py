@@ -193,3 +193,33 @@ def test_compile_model_argument_checks(tmp_path):
         compile_model(m, (x,), output_dir=str(tmp_path), autotune=True, kernel_variant="naive_ijk")
     with pytest.raises(ValueError):
         compile_model(m, (x,), output_dir=str(tmp_path), autotune=False, gpu_kernel="triton")
+
+
+REFERENCE_PY = "/root/reference/python"
+
+
+@pytest.mark.skipif(not os.path.isdir(REFERENCE_PY), reason="reference checkout not present")
+def test_reference_native_runtime_binds_artifact(tiny_compiled):
+    """The reference's own ctypes loader (python/forgetune/runtime.py) binds a
+    compiled artifact unchanged: same symbols, same contract checks."""
+    import importlib
+    import sys
+    sys.path.insert(0, REFERENCE_PY)
+    try:
+        ref_runtime = importlib.import_module("forgetune.runtime")
+        ref_errors = importlib.import_module("forgetune.errors")
+    finally:
+        sys.path.remove(REFERENCE_PY)
+    so = tiny_compiled.manifest()["artifacts"]["shared_library"]
+    rt = ref_runtime.NativeRuntime(so, (-1, 784), (-1, 10))
+    assert rt.is_dynamic and rt.max_batch_size == 128
+    with pytest.raises(ref_errors.InvalidShapeError):
+        rt.run(np.ones((129, 784), np.float32))
+    with pytest.raises(TypeError):
+        rt.run(np.ones((2, 784), np.float64))
+    x = np.ones((2, 784), np.float32)
+    if _native.device_count() == 0:
+        with pytest.raises(ref_errors.ForgeTuneRuntimeError, match="-5"):
+            rt.run(x)
+    else:
+        np.testing.assert_array_equal(rt.run(x), tiny_compiled.run(x))
