@@ -28,6 +28,7 @@
 #include "engine.hpp"
 #include "philox.cuh"
 #include "simt_gemm.cuh"
+#include "splitk_gemv.cuh"
 #include "tc_gemm.cuh"
 
 #define FTB_API extern "C" __attribute__((visibility("default")))
@@ -102,6 +103,9 @@ struct ExecCtx {
   std::vector<cudaEvent_t> ev_in, ev_out;  // per pipeline chunk
   cudaEvent_t ev_a = nullptr, ev_b = nullptr;
   std::vector<cudaEvent_t> prof;  // [slot][step + 1] step-boundary events
+  // split-K workspace inside the block: partial sums and per-column-block tickets
+  float* ws_part = nullptr;
+  unsigned* ws_tickets = nullptr;
   bool in_use = false;
   struct CachedGraph {
     int64_t batch;
@@ -327,17 +331,35 @@ static int layout_block(Model* m, ExecCtx* c, size_t min_bytes, bool* did_alloc)
   const size_t in_b = round256((size_t)p.max_batch * p.in_static_elems * sizeof(float));
   const size_t out_rows = p.output_dynamic ? (size_t)p.max_batch : 1;
   const size_t out_b = round256(out_rows * p.out_static_elems * sizeof(float));
-  const size_t need = std::max(arena + in_b + out_b, min_bytes);
+  // split-K workspace sized for the widest GEMM: up to 64 slices x 16 rows x N
+  int64_t max_n = 0;
+  for (const Step& st : p.steps)
+    if (st.kind == ST_GEMM) max_n = std::max(max_n, st.N);
+  const size_t part_b = round256((size_t)kSkMaxSlices * 16 * (size_t)max_n * sizeof(float));
+  const size_t tick_b = round256((size_t)((max_n + kSkCols - 1) / kSkCols + 1) * sizeof(unsigned));
+  const size_t need = std::max(arena + in_b + out_b + part_b + tick_b, min_bytes);
+  bool fresh = false;
   if (!c->block || c->block_bytes < need) {
     int rc = alloc_block(c, need);
     if (rc) return rc;
     if (did_alloc) *did_alloc = true;
+    fresh = true;
     for (auto& cg : c->graphs) cudaGraphExecDestroy(cg.exec);
     c->graphs.clear();
   }
   c->arena = c->block;
   c->d_in = reinterpret_cast<float*>(c->block + arena);
   c->d_out = reinterpret_cast<float*>(c->block + arena + in_b);
+  c->ws_part = max_n ? reinterpret_cast<float*>(c->block + arena + in_b + out_b) : nullptr;
+  c->ws_tickets = max_n ? reinterpret_cast<unsigned*>(c->block + arena + in_b + out_b + part_b) : nullptr;
+  if (fresh && c->ws_tickets) {
+    // tickets start at zero; every split-K launch leaves them at zero
+    if (cudaMemset(c->ws_tickets, 0, tick_b) != cudaSuccess) {
+      cudaGetLastError();
+      set_error("workspace initialisation failed");
+      return ST_DEVICE;
+    }
+  }
   return ST_OK;
 }
 
@@ -445,8 +467,9 @@ static void copy_floats(const float* a, float* y, int64_t n, int sm, cudaStream_
 // Enqueues the launch list for `batch` rows on stream s.  With `marks`
 // (steps + 1 events) an event is recorded before every step and after the
 // last one, so per-step device times can be read back afterwards.
-static int enqueue(const Model* m, const Replica* rep, char* arena, const float* in, float* out, int64_t batch,
+static int enqueue(const Model* m, const Replica* rep, ExecCtx* c, const float* in, float* out, int64_t batch,
                    cudaStream_t s, cudaEvent_t* marks = nullptr) {
+  char* arena = c->arena;
   const int policy = m->prog.graph.kernel_policy;
   const bool exact = policy == KP_SIMT_EXACT;
   auto ptr = [&](const Operand& o) -> float* {
@@ -488,6 +511,26 @@ static int enqueue(const Model* m, const Replica* rep, char* arena, const float*
             dispatch_simt<false, true>(a, sm, s);
         } else {
           const TcWeights& tw = rep->tc[i];
+          if (!exact && M <= 16 && c->ws_part && policy != KP_TCGEN05) {
+            SplitKArgs sk{};
+            sk.A = a.A;
+            sk.B = a.B;
+            sk.bias = a.bias;
+            sk.res = a.res;
+            sk.Y = a.Y;
+            sk.part = c->ws_part;
+            sk.tickets = c->ws_tickets;
+            sk.M = (int)M;
+            sk.N = (int)st.N;
+            sk.K = (int)st.K;
+            sk.epi = st.epi;
+            const int rc = launch_splitk(sk, sm, s);
+            if (rc < 0) {
+              set_error(std::string("split-K GEMM launch failed: ") + cudaGetErrorString(cudaGetLastError()));
+              return ST_DEVICE;
+            }
+            if (rc == 0) break;
+          }
           const bool tc_ok = tw.maps_ready && !exact &&
                              (policy == KP_TCGEN05 || (policy == KP_AUTO && tc_gemm_profitable(M, st.K, st.N)));
           int tc_rc = 1;  // 1: not taken
@@ -621,7 +664,7 @@ static int run_graph(Model* m, Replica* rep, ExecCtx* c, const float* in, float*
     }
   cudaGraph_t graph = nullptr;
   CUDA_TRY(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
-  int rc = enqueue(m, rep, c->arena, in, out, batch, c->stream);
+  int rc = enqueue(m, rep, c, in, out, batch, c->stream);
   cudaError_t e = cudaStreamEndCapture(c->stream, &graph);
   if (rc) {
     if (graph) cudaGraphDestroy(graph);
@@ -706,7 +749,7 @@ static int run_host_one(Model* m, int dev, const float* in, float* out, int64_t 
     const int64_t r0 = k * cr, r1 = std::min(batch, r0 + cr);
     CUDA_TRY(cudaStreamWaitEvent(c->stream, c->ev_in[k], 0));
     // chunks are thousands of rows: launch directly, no graph per chunk address
-    rc = enqueue(m, rep, c->arena, c->d_in + r0 * fi, c->d_out + r0 * fo, r1 - r0, c->stream);
+    rc = enqueue(m, rep, c, c->d_in + r0 * fi, c->d_out + r0 * fo, r1 - r0, c->stream);
     if (rc) return rc;
     CUDA_TRY(cudaEventRecord(c->ev_out[k], c->stream));
     CUDA_TRY(cudaStreamWaitEvent(c->d2h, c->ev_out[k], 0));
@@ -996,7 +1039,7 @@ FTB_API int ftb_model_run_device_profiled(void* handle, const float* d_in, size_
     c->prof.push_back(e);
   }
   cudaStream_t s = static_cast<cudaStream_t>(stream);  // NULL: the legacy default stream
-  return enqueue(m, rep, c->arena, d_in, d_out, batch, s, c->prof.data() + per * slot);
+  return enqueue(m, rep, c, d_in, d_out, batch, s, c->prof.data() + per * slot);
 }
 
 // Waits for the events of `slot` and writes each step's device time (ms).
