@@ -98,13 +98,15 @@ def test_run_to_run_and_batch_invariance(policy, tmp_root):
     b = cm.run(x)
     assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
     # Rows are independent in every kernel, so the same rows inside a batch
-    # that selects the same kernels give the same bits.  Under "auto" small
-    # batches run on SIMT and large ones on the tensor cores, so only the
-    # single-family policies are checked across all sizes.
-    if policy in ("simt", "simt_exact"):
-        for lo, hi in ((0, 1), (100, 357), (4096, 8192), (65000, 65536)):
-            part = cm.run(np.ascontiguousarray(x[lo:hi]))
-            assert np.array_equal(part.view(np.uint32), a[lo:hi].view(np.uint32)), (lo, hi)
+    # that selects the same kernels give the same bits.  "simt_exact" uses one
+    # kernel family for every size; "simt" uses the split-K kernel up to 16
+    # rows and register tiles above; "auto" adds the tensor cores from 1024.
+    slices = {"simt_exact": ((0, 1), (100, 357), (4096, 8192), (65000, 65536)),
+              "simt": ((100, 357), (4096, 8192), (65000, 65536)),
+              "auto": (), "tcgen05": ()}[policy]
+    for lo, hi in slices:
+        part = cm.run(np.ascontiguousarray(x[lo:hi]))
+        assert np.array_equal(part.view(np.uint32), a[lo:hi].view(np.uint32)), (lo, hi)
 
 
 def test_unfused_graph_matches_oracle(tmp_path):
