@@ -45,6 +45,8 @@ _SIGS = {
     "ftb_model_describe": ([c_void_p, c_void_p, c_size_t], c_int),
     "ftb_device_count": ([], c_int),
     "ftb_philox_normal": ([c_void_p, c_uint64, c_uint64, c_uint64, c_void_p], c_int),
+    "ftb_small_gemm_noalloc": ([c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64,
+                                ctypes.c_uint32, c_void_p], c_int),
 }
 
 EXPORTED = sorted(_SIGS)

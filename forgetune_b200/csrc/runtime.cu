@@ -26,6 +26,7 @@
 
 #include "elementwise.cuh"
 #include "engine.hpp"
+#include "forgetune_b200.h"
 #include "philox.cuh"
 #include "simt_gemm.cuh"
 #include "splitk_gemv.cuh"
@@ -1199,5 +1200,124 @@ FTB_API int ftb_philox_normal(float* d_out, uint64_t seed, uint64_t first, uint6
   const unsigned grid = (unsigned)std::min<uint64_t>((blocks + 255) / 256, (uint64_t)sm * 16);
   philox_normal_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(d_out, seed, first, count);
   CUDA_TRY(cudaGetLastError());
+  return ST_OK;
+}
+
+// ===========================================================================
+// Split-K GEMM for up to 16 rows that allocates nothing
+// ===========================================================================
+// Some callers cannot allocate device memory where they call us: a plugin
+// running inside another engine's execution step (an inference server or
+// graph runtime that owns all device memory and forbids allocation there), or
+// a latency-critical loop that cannot afford cudaMalloc's implicit device
+// synchronisation.  ftb_small_gemm_noalloc gives them the split-K kernel with
+// its scratch -- the slice partial sums and the per-column-block tickets -- in
+// one file-scope __device__ array of fixed size instead of a context arena.
+// Every GPU on which this library's module is loaded holds that array
+// (4 MiB + 4 KiB) until the process exits.  All calls on a device share it and
+// it keeps the previous call's partial sums; the tickets, which must start at
+// zero, are cleared by every call.  Calls that overlap on the GPU (unordered
+// streams) race on the shared array.
+namespace ftb {
+constexpr size_t kNoAllocPartFloats = size_t(1) << 20;  // 4 MiB of partial sums
+constexpr int kNoAllocTickets = 1024;                    // N up to 65536
+struct NoAllocScratch {
+  float part[kNoAllocPartFloats];
+  unsigned tickets[kNoAllocTickets];
+};
+}  // namespace ftb
+
+static __device__ __align__(256) ftb::NoAllocScratch g_noalloc_scratch;
+
+namespace ftb {
+constexpr int kNoAllocMaxDevices = 64;
+struct NoAllocDevice {
+  std::once_flag once;
+  int rc = ST_OK;
+  std::string err;
+  NoAllocScratch* scratch = nullptr;  // device address of g_noalloc_scratch on this device
+  int sm_count = 0;
+};
+static NoAllocDevice g_noalloc_devices[kNoAllocMaxDevices];
+
+// One-time set-up for `dev`, which is the current device: the device address
+// of the scratch array (in host code the array's name is only a host-side
+// stand-in) and the shared-memory attribute of the kernels it launches.
+static void noalloc_setup(int dev, NoAllocDevice* d) {
+  void* p = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+  if (e != cudaSuccess) {
+    d->rc = ST_DEVICE;
+    d->err = std::string("cudaGetSymbolAddress of the split-K scratch failed: ") + cudaGetErrorString(e);
+    cudaGetLastError();
+    return;
+  }
+  d->scratch = static_cast<NoAllocScratch*>(p);
+  if (cudaDeviceGetAttribute(&d->sm_count, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+      cudaFuncSetAttribute(splitk_gemv_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024) !=
+          cudaSuccess ||
+      cudaFuncSetAttribute(splitk_gemv_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024) !=
+          cudaSuccess) {
+    d->rc = ST_DEVICE;
+    d->err = std::string("split-K kernel set-up failed: ") + cudaGetErrorString(cudaGetLastError());
+  }
+}
+}  // namespace ftb
+
+FTB_API int ftb_small_gemm_noalloc(const float* d_x, const float* d_w, const float* d_bias, const float* d_residual,
+                                   float* d_y, int64_t m, int64_t k, int64_t n, uint32_t flags, void* stream) {
+  if (!d_x || !d_w || !d_y) return ST_NULL;
+  if (((flags & FTB_SMALL_GEMM_BIAS) && !d_bias) || ((flags & FTB_SMALL_GEMM_RESIDUAL) && !d_residual))
+    return ST_NULL;
+  if (m < 1 || m > 16 || k < 1 || n < 1 || k > (1 << 30) || n > (1 << 30)) {
+    set_error("ftb_small_gemm_noalloc: needs 1 <= m <= 16 and positive k, n");
+    return ST_INPUT;
+  }
+  if ((flags & FTB_SMALL_GEMM_RESIDUAL) && k != n) {
+    set_error("ftb_small_gemm_noalloc: a residual needs k == n");
+    return ST_INPUT;
+  }
+  int dev = 0;
+  CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kNoAllocMaxDevices) {
+    set_error("ftb_small_gemm_noalloc: device ordinal beyond the supported range");
+    return ST_CONFIG;
+  }
+  NoAllocDevice& d = g_noalloc_devices[dev];
+  std::call_once(d.once, [&]() { noalloc_setup(dev, &d); });
+  if (d.rc != ST_OK) {
+    set_error(d.err);
+    return d.rc;
+  }
+  int ks = 0, kc = 0;
+  splitk_shape(k, n, d.sm_count, &ks, &kc);
+  const size_t need = (size_t)ks * 16 * (size_t)n;
+  const int64_t blocks = (n + kSkCols - 1) / kSkCols;
+  if (need > kNoAllocPartFloats || blocks > kNoAllocTickets) {
+    set_error("ftb_small_gemm_noalloc: k=" + std::to_string(k) + ", n=" + std::to_string(n) + " needs " +
+              std::to_string(need) + " floats of partial sums; the fixed scratch holds " +
+              std::to_string(kNoAllocPartFloats));
+    return ST_INPUT;
+  }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  CUDA_TRY(cudaMemsetAsync(d.scratch->tickets, 0, sizeof(unsigned) * (size_t)blocks, s));
+  SplitKArgs a{};
+  a.A = d_x;
+  a.B = d_w;
+  a.bias = d_bias;
+  a.res = d_residual;
+  a.Y = d_y;
+  a.part = d.scratch->part;
+  a.tickets = d.scratch->tickets;
+  a.M = (int)m;
+  a.N = (int)n;
+  a.K = (int)k;
+  a.epi = ((flags & FTB_SMALL_GEMM_BIAS) ? EPI_BIAS_LAST : 0u) | ((flags & FTB_SMALL_GEMM_RELU) ? EPI_RELU_PRE : 0u) |
+          ((flags & FTB_SMALL_GEMM_RESIDUAL) ? EPI_RESIDUAL : 0u);
+  const int rc = launch_splitk(a, d.sm_count, s);
+  if (rc != 0) {
+    set_error(std::string("ftb_small_gemm_noalloc: launch failed: ") + cudaGetErrorString(cudaGetLastError()));
+    return ST_DEVICE;
+  }
   return ST_OK;
 }

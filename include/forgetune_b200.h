@@ -152,6 +152,32 @@ FORGETUNE_EXPORT int ftb_device_count(void);
  * seed, written to device memory on `stream` (the wide-MLP input generator). */
 FORGETUNE_EXPORT int ftb_philox_normal(float* d_out, uint64_t seed, uint64_t first, uint64_t count, void* stream);
 
+/* Small-batch GEMM that allocates nothing.  No counterpart in the reference
+ * (whose runtime is CPU-only): it is for callers that cannot allocate device
+ * memory where they call in -- a plugin inside another engine's execution
+ * step, whose host owns all device memory, or a latency-critical loop that
+ * cannot take cudaMalloc's device synchronisation.
+ *
+ *   y[m, n] = epi( sum_k x[m, k] w[k, n] ),  x [m, k], w [k, n], y [m, n]
+ *   row-major fp32 device arrays on the current device; flags select, in this
+ *   order, + bias[n] (FTB_SMALL_GEMM_BIAS), ReLU that keeps NaN
+ *   (FTB_SMALL_GEMM_RELU), + residual[m, n] (FTB_SMALL_GEMM_RESIDUAL, k == n).
+ *
+ * 1 <= m <= 16.  The split-K scratch is a fixed 4 MiB array in the library
+ * (held on every GPU that loads it until exit): requests whose partial sums do
+ * not fit (about 16 * n * ceil(k / 512) floats or more) return -2 with a
+ * message in ftb_last_error().  Enqueued on `stream` (NULL = legacy default
+ * stream) without synchronising.  The first call on a device looks up the
+ * scratch array's device address and sets kernel attributes; make that first
+ * call before any stream capture.  Every call shares the scratch, so calls
+ * that overlap on the GPU race on it; calls ordered on one stream do not. */
+#define FTB_SMALL_GEMM_BIAS 1u
+#define FTB_SMALL_GEMM_RELU 2u
+#define FTB_SMALL_GEMM_RESIDUAL 4u
+FORGETUNE_EXPORT int ftb_small_gemm_noalloc(const float* d_x, const float* d_w, const float* d_bias,
+                                            const float* d_residual, float* d_y, int64_t m, int64_t k, int64_t n,
+                                            uint32_t flags, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
