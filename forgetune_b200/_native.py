@@ -31,6 +31,7 @@ _SIGS = {
     "ftb_model_set_policy": ([c_void_p, c_int], c_int),
     "ftb_model_prepare": ([c_void_p], c_int),
     "ftb_model_set_step_config": ([c_void_p, c_int, c_int, c_int, c_int], c_int),
+    "ftb_model_set_fault_injection": ([c_void_p, c_int], c_int),
     "ftb_model_run": ([c_void_p, c_void_p, c_size_t, c_void_p, c_size_t, c_int64, c_int], c_int),
     "ftb_model_run_device": ([c_void_p, c_void_p, c_size_t, c_void_p, c_size_t, c_int64, c_void_p], c_int),
     "ftb_model_run_device_profiled": ([c_void_p, c_void_p, c_size_t, c_void_p, c_size_t, c_int64, c_void_p, c_int],

@@ -146,6 +146,7 @@ struct Model {
   std::mutex mu;
   std::atomic<size_t> process_allocs{0};
   bool allow_tc = true;
+  std::atomic<int> tc_stall_test{0};  // failure-detection hook, see ftb_model_set_fault_injection
 };
 
 static void destroy_ctx(ExecCtx* c) {
@@ -548,6 +549,7 @@ static int enqueue(const Model* m, const Replica* rep, ExecCtx* c, const float* 
             t.K = st.K;
             t.Kp = tw.Kp;
             t.epi = st.epi;
+            t.stall_test = m->tc_stall_test.load();
             TcConfig cfg;
             cfg.bn = st.tc_bn;
             cfg.bk = st.tc_bk;
@@ -730,6 +732,7 @@ static int run_host_one(Model* m, int dev, const float* in, float* out, int64_t 
   if (!chunked) {
     const size_t in_b = (size_t)(p.dynamic ? batch : 1) * p.in_static_elems * 4;
     const size_t out_b = (size_t)(p.output_dynamic ? batch : 1) * p.out_static_elems * 4;
+    *rep->err_host = 0;  // the previous synchronous run on this replica has finished
     CUDA_TRY(cudaMemcpyAsync(c->d_in, in, in_b, cudaMemcpyHostToDevice, c->stream));
     rc = run_graph(m, rep, c, c->d_in, c->d_out, batch, c->stream);
     if (rc) return rc;
@@ -737,6 +740,7 @@ static int run_host_one(Model* m, int dev, const float* in, float* out, int64_t 
     CUDA_TRY(cudaStreamSynchronize(c->stream));
     return check_kernel_error(rep);
   }
+  *rep->err_host = 0;
   const int64_t cr = chunk_rows_for(p, batch);
   const int64_t nch = (batch + cr - 1) / cr;
   const int64_t fi = p.in_static_elems, fo = p.out_static_elems;
@@ -936,6 +940,22 @@ FTB_API int ftb_model_set_step_config(void* handle, int step, int tc_bn, int tc_
   };
   apply(m->prog.steps[(size_t)step]);
   for (auto& rep : m->replicas) apply(rep->steps[(size_t)step]);
+  for (ExecCtx* c : m->all_ctxs) {
+    for (auto& cg : c->graphs) cudaGraphExecDestroy(cg.exec);
+    c->graphs.clear();
+  }
+  return ST_OK;
+}
+
+// Failure-detection hook: while `tc_stall` is non-zero, every tensor-core
+// launch of this model first waits on a barrier that nothing completes; the
+// bounded wait runs out (about 2 s), the kernel aborts cleanly and the
+// synchronous run returns -5.  No fault, trap or unbounded wait is involved.
+FTB_API int ftb_model_set_fault_injection(void* handle, int tc_stall) {
+  auto* m = static_cast<Model*>(handle);
+  if (!m) return ST_NULL;
+  m->tc_stall_test.store(tc_stall ? 1 : 0);
+  std::lock_guard<std::mutex> lk(m->mu);
   for (ExecCtx* c : m->all_ctxs) {
     for (auto& cg : c->graphs) cudaGraphExecDestroy(cg.exec);
     c->graphs.clear();

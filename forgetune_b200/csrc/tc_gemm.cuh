@@ -67,6 +67,7 @@ struct TcArgs {
   int64_t M, N, K, Kp;
   uint32_t epi;
   TcHead head;
+  int stall_test;
 };
 
 struct TcKernelParams {
@@ -77,6 +78,9 @@ struct TcKernelParams {
   uint32_t epi;
   TcHead head;
   int* err;  // device error word: 0 ok, nonzero = a bounded wait gave up
+  // test hook: the MMA thread first waits on a barrier nothing completes, so
+  // the bounded wait runs out and the abort path runs (failure-detection tests)
+  int stall_test;
 };
 
 constexpr int kTcMaxHeadN = 16;
@@ -147,16 +151,16 @@ __device__ __forceinline__ uint64_t global_ns() {
 constexpr uint64_t kTcWaitLimitNs = 2000000000ull;  // 2 s per wait: far beyond any legitimate stall
 
 // Bounded wait.  Returns false (and raises the CTA abort flag and the device
-// error word) if the phase did not complete within the limit, or if another
-// role of this CTA already aborted.
+// error word) if the phase did not complete within the limit, or, unless
+// `ignore_abort`, if another role of this CTA already aborted.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* err,
-                                          int code) {
+                                          int code, bool ignore_abort = false) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_ns();
   for (uint32_t it = 1;; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((it & 255u) == 0) {
-      if (*abort_flag) return false;
+      if (!ignore_abort && *abort_flag) return false;
       if (global_ns() - t0 > kTcWaitLimitNs) {
         *abort_flag = 1;
         atomicCAS(err, 0, code);
@@ -243,7 +247,7 @@ struct TcSmem {
   static constexpr int EPI_BYTES = 4 * 32 * 33 * 4;       // per epilogue warp: a 32 x 32 transpose tile
   // head weights [256][16], this GEMM's bias [256], the head's bias [16]
   static constexpr int HEAD_BYTES = (kTcMaxHeadK * kTcMaxHeadN + kTcMaxHeadK + kTcMaxHeadN) * 4;
-  static constexpr int NBAR = 3 * STAGES + 5;
+  static constexpr int NBAR = 3 * STAGES + 6;
   static constexpr int BAR_BYTES = 8 * NBAR + 16;
   static constexpr int TOTAL = 1024 + STAGES * STAGE_BYTES + EPI_BYTES + HEAD_BYTES + BAR_BYTES;
 };
@@ -270,8 +274,9 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
   uint64_t* accf = bars + 3 * STAGES;   // [2] accumulator buffer complete
   uint64_t* acce = accf + 2;            // [2] accumulator buffer drained by the epilogue
   uint64_t* drain = acce + 2;           // MMAs retired after an abort
-  volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(drain + 1);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(drain + 1) + 1;
+  uint64_t* never = drain + 1;          // never arrived on (stall_test)
+  volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(never + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(never + 1) + 1;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -291,6 +296,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
       mbar_init(&acce[b], 4);
     }
     mbar_init(drain, 1);
+    mbar_init(never, 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -330,6 +336,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
       const uint32_t idesc = idesc_tf32<BN>();
       uint32_t it = 0, tc = 0;
       bool ok = true;
+      if (p.stall_test) ok = mbar_wait(never, 0, abort_flag, p.err, 9);
       for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x, ++tc) {
         const uint32_t buf = tc & 1u, use = tc >> 1;
         if (!(ok = mbar_wait(&acce[buf], (use & 1u) ^ 1u, abort_flag, p.err, 2))) break;
@@ -357,8 +364,10 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
         if (ok) umma_commit(&accf[buf]);
       }
       if (!ok) {
-        umma_commit(drain);  // every MMA issued so far retires before this arrives
-        mbar_wait(drain, 0, abort_flag, p.err, 5);
+        // every MMA issued so far retires before this arrives; wait for it
+        // even though the CTA is aborting, so TMEM is not freed under them
+        umma_commit(drain);
+        mbar_wait(drain, 0, abort_flag, p.err, 5, /*ignore_abort=*/true);
       }
     }
   } else if (warp < 6) {
@@ -573,6 +582,7 @@ inline int launch_tc_bn(const TcArgs& t, const TcWeights& w, int* err, int sm_co
   p.epi = t.epi;
   p.head = t.head;
   p.err = err;
+  p.stall_test = t.stall_test;
   // the accumulator starts at zero: a bias-first epilogue adds the bias at the end
   if (p.epi & EPI_BIAS_FIRST) p.epi = (p.epi & ~(uint32_t)EPI_BIAS_FIRST) | EPI_BIAS_LAST;
   if (p.head.epi & EPI_BIAS_FIRST) p.head.epi = (p.head.epi & ~(uint32_t)EPI_BIAS_FIRST) | EPI_BIAS_LAST;

@@ -126,6 +126,11 @@ FORGETUNE_EXPORT int ftb_model_set_policy(void* model, int policy);
  * fused into its epilogue.  For the autotuner; call between runs. */
 FORGETUNE_EXPORT int ftb_model_set_step_config(void* model, int step, int tc_bn, int tc_bk, int fuse_head);
 FORGETUNE_EXPORT int ftb_model_prepare(void* model);
+/* Failure-detection hook (tests): while tc_stall != 0 every tensor-core
+ * launch of the model makes one pipeline wait that nothing completes run out
+ * (about 2 s); the kernel aborts cleanly and a synchronous run returns -5.
+ * The context stays usable once the hook is cleared. */
+FORGETUNE_EXPORT int ftb_model_set_fault_injection(void* model, int tc_stall);
 FORGETUNE_EXPORT int ftb_model_run(void* model, const float* input, size_t input_count, float* output,
                                    size_t output_count, int64_t batch_size, int api);
 FORGETUNE_EXPORT int ftb_model_run_device(void* model, const float* d_input, size_t input_count, float* d_output,

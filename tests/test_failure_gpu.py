@@ -1,0 +1,48 @@
+"""Failure detection without a GPU fault.
+
+The tensor-core kernel bounds every mbarrier wait.  A test hook makes the MMA
+thread wait on a barrier that nothing completes: the wait runs out (~2 s), the
+kernel raises its abort flag, drains, frees its TMEM and returns; the host
+reads the mapped error word and the run returns -5 with a message.  The same
+context then runs correctly again.  No trap, bad address or unbounded wait is
+used.
+"""
+
+import numpy as np
+import pytest
+import torch
+import torch.nn as nn
+
+from forgetune_b200 import _native, compile_model
+from oracle import oracle
+
+pytestmark = pytest.mark.gpu
+
+
+def test_tensor_core_wait_timeout_is_reported_and_recoverable(tmp_path):
+    torch.manual_seed(3)
+    m = nn.Sequential(nn.Linear(256, 128), nn.ReLU()).eval()
+    cm = compile_model(m, (torch.randn(2, 256),), output_dir=str(tmp_path), autotune=False, enable_fusion=True,
+                       kernel_variant="fused_ikj", dynamic_batch=True, max_batch_size=4096,
+                       gpu_kernel="tcgen05", verify=False)
+    with open(cm.manifest()["artifacts"]["graph_blob"], "rb") as f:
+        eng = _native.EngineModel(f.read())
+    eng.set_devices([torch.cuda.current_device()])
+    x = np.random.default_rng(0).standard_normal((2048, 256)).astype(np.float32)
+    y = np.zeros((2048, 128), np.float32)
+    assert eng.run(x, y) == 0
+    want = oracle.run_model(m, x, "naive_ijk")
+    assert np.allclose(y, want, atol=1e-4, rtol=1e-4)
+
+    lib = _native.lib()
+    assert lib.ftb_model_set_fault_injection(eng.handle, 1) == 0
+    y[:] = 0
+    rc = eng.run(x, y)
+    assert rc == -5
+    assert "exceeded its limit" in _native.last_error()
+
+    assert lib.ftb_model_set_fault_injection(eng.handle, 0) == 0
+    assert eng.run(x, y) == 0, _native.last_error()
+    assert np.allclose(y, want, atol=1e-4, rtol=1e-4)
+    eng.close()
+    cm.close()
