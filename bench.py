@@ -213,26 +213,17 @@ def run_ours(args) -> int:
     import torch
     import torch.distributed as dist
 
-    from forgetune_b200 import _native, compile_model, workloads
-    from forgetune_b200.graph_blob import POLICIES
+    from forgetune_b200 import _native, compile_model, sharding, workloads
 
-    rank, world, local = env_int("RANK", 0), env_int("WORLD_SIZE", 1), env_int("LOCAL_RANK", 0)
+    rank, world, local = sharding.rank_info()
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
-        from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
-
-    def barrier():
-        if world > 1:
-            dist.barrier()
+        sharding.init("nccl", dev)
+    barrier = sharding.barrier
 
     def max_over_ranks(v: float) -> float:
-        if world == 1:
-            return v
-        t = torch.tensor([v], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+        return sharding.max_over_ranks(v, dev)
 
     B = args.batch
     model = workloads.tiny_mlp()
@@ -249,7 +240,8 @@ def run_ours(args) -> int:
     stream = torch.cuda.current_stream(dev)
     x = torch.empty(B * IN_F, dtype=torch.float32, device=dev)
     y = torch.empty(B * OUT_F, dtype=torch.float32, device=dev)
-    _native.philox_normal(x.data_ptr(), 1, rank * B * IN_F, B * IN_F, stream.cuda_stream)
+    _native.philox_normal(x.data_ptr(), 1, sharding.shard_element_offset(rank, B, IN_F), B * IN_F,
+                          stream.cuda_stream)
     torch.cuda.synchronize()
 
     def step(slot):
