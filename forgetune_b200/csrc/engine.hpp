@@ -189,6 +189,7 @@ struct Step {
   // whether a head may be fused (set by the autotuner or the caller)
   int32_t tc_bn = 0;
   int32_t tc_bk = 0;
+  int32_t tc_mh = 0;  // 128-row halves per tile (0 = by shape)
   bool fuse_head = true;
 };
 

@@ -238,9 +238,10 @@ __device__ __forceinline__ float tf32_rna(float v) {
         "=r"(r[30]), "=r"(r[31])                                                                             \
       : "r"(taddr))
 
-template <int BN, int BK, int STAGES>
+template <int BN, int BK, int STAGES, int MH>
 struct TcSmem {
-  static constexpr int A_BYTES = kTcBM * BK * 4;
+  static constexpr int A_HALF_BYTES = kTcBM * BK * 4;  // one 128-row half of the A tile
+  static constexpr int A_BYTES = MH * A_HALF_BYTES;
   static constexpr int B_BYTES = BN * BK * 4;
   static constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
   static constexpr int TX_BYTES = A_BYTES + 2 * B_BYTES;  // what TMA writes per stage
@@ -252,13 +253,16 @@ struct TcSmem {
   static constexpr int TOTAL = 1024 + STAGES * STAGE_BYTES + EPI_BYTES + HEAD_BYTES + BAR_BYTES;
 };
 
-template <int BN, int BK, int STAGES>
+template <int BN, int BK, int STAGES, int MH>
 __global__ void __launch_bounds__(kTcThreads, 1)
 tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_bhi,
                const __grid_constant__ CUtensorMap map_blo, TcKernelParams p) {
-  using L = TcSmem<BN, BK, STAGES>;
+  using L = TcSmem<BN, BK, STAGES, MH>;
   static_assert(L::TOTAL <= 227 * 1024, "shared memory budget");
-  static_assert(2 * BN <= 512, "two accumulators must fit in TMEM");
+  static_assert(MH == 1 || MH == 2, "tiles of 128 or 256 rows");
+  static_assert(2 * MH * BN <= 512, "two accumulators of MH x BN columns must fit in TMEM");
+  constexpr int BMT = kTcBM * MH;          // rows per tile
+  constexpr uint32_t TMEM_COLS = 2 * MH * BN;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   auto a_tile = [&](int s) { return reinterpret_cast<float*>(smem + s * L::STAGE_BYTES); };
@@ -280,7 +284,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int tiles_m = (p.M + kTcBM - 1) / kTcBM;
+  const int tiles_m = (p.M + BMT - 1) / BMT;
   const int tiles_n = (p.N + BN - 1) / BN;
   const int ntiles = tiles_m * tiles_n;
   const int nk = (p.K + BK - 1) / BK;
@@ -303,7 +307,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_u32(const_cast<uint32_t*>(tmem_slot))),
-                 "r"((uint32_t)(2 * BN))
+                 "r"(TMEM_COLS)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
@@ -318,7 +322,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
       uint32_t it = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
-        const int m0 = (t / tiles_n) * kTcBM;
+        const int m0 = (t / tiles_n) * BMT;
         const int n0 = (t % tiles_n) * BN;
         for (int kb = 0; kb < nk; ++kb, ++it) {
           const int s = (int)(it % STAGES);
@@ -341,7 +345,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
         const uint32_t buf = tc & 1u, use = tc >> 1;
         if (!(ok = mbar_wait(&acce[buf], (use & 1u) ^ 1u, abort_flag, p.err, 2))) break;
         tc_fence_after();
-        const uint32_t d = tmem + buf * (uint32_t)BN;
+        const uint32_t d = tmem + buf * (uint32_t)(MH * BN);
         for (int kb = 0; kb < nk; ++kb, ++it) {
           const int s = (int)(it % STAGES);
           const uint32_t par = (it / STAGES) & 1u;
@@ -353,11 +357,16 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
 #pragma unroll
           for (int j = 0; j < BK / 8; ++j) {  // K = 8 tf32 (32 bytes) per MMA
             const uint32_t off = (uint32_t)j * 32u;
-            const uint64_t dah = smem_desc_sw<BK>(ahi + off), dal = smem_desc_sw<BK>(alo + off);
             const uint64_t dbh = smem_desc_sw<BK>(bhi + off), dbl = smem_desc_sw<BK>(blo + off);
-            umma_tf32(d, dah, dbh, idesc, (kb > 0 || j > 0) ? 1u : 0u);
-            umma_tf32(d, dah, dbl, idesc, 1u);
-            umma_tf32(d, dal, dbh, idesc, 1u);
+#pragma unroll
+            for (int h = 0; h < MH; ++h) {  // each 128-row half of the tile against the same W k-block
+              const uint32_t ao = off + (uint32_t)(h * L::A_HALF_BYTES);
+              const uint64_t dah = smem_desc_sw<BK>(ahi + ao), dal = smem_desc_sw<BK>(alo + ao);
+              const uint32_t dh = d + (uint32_t)(h * BN);
+              umma_tf32(dh, dah, dbh, idesc, (kb > 0 || j > 0) ? 1u : 0u);
+              umma_tf32(dh, dah, dbl, idesc, 1u);
+              umma_tf32(dh, dal, dbh, idesc, 1u);
+            }
           }
           umma_commit(&empty[s]);
         }
@@ -382,7 +391,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
         float4* hi = reinterpret_cast<float4*>(a_tile(s));
         float4* lo = reinterpret_cast<float4*>(alo_tile(s));
 #pragma unroll
-        for (int i = 0; i < (kTcBM * BK / 4) / 128; ++i) {
+        for (int i = 0; i < (BMT * BK / 4) / 128; ++i) {
           const int idx = t128 + i * 128;
           const float4 v = hi[idx];
           float4 h, l;
@@ -428,9 +437,11 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
       const uint32_t buf = tc & 1u, use = tc >> 1;
       if (!mbar_wait(&accf[buf], use & 1u, abort_flag, p.err, 7)) break;
       tc_fence_after();
-      const int m0 = (t / tiles_n) * kTcBM;
       const int n0 = (t % tiles_n) * BN;
-      const uint32_t base = tmem + buf * (uint32_t)BN + ((uint32_t)(q * 32) << 16);
+#pragma unroll 1
+      for (int h = 0; h < MH; ++h) {
+      const int m0 = (t / tiles_n) * BMT + h * kTcBM;
+      const uint32_t base = tmem + (buf * MH + h) * (uint32_t)BN + ((uint32_t)(q * 32) << 16);
       if (hn > 0) {
         // the tile holds whole rows (N <= BN): lane = row, accumulate the head
         const int m = m0 + q * 32 + lane;
@@ -469,9 +480,6 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
             if (o < hn)
               p.head.y[(int64_t)m * hn + o] = apply_epilogue(acc[o], p.head.epi, head_bb, nullptr, m, o, hn);
         }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&acce[buf]);
         continue;
       }
 #pragma unroll 1
@@ -493,6 +501,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
           }
         }
       }
+      }  // halves
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acce[buf]);
@@ -503,8 +512,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)(2 * BN))
-                 : "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
   }
 }
 
@@ -560,18 +568,18 @@ inline bool tc_prepare_weights(TcWeights& w, int64_t N) {
 
 // Returns 0 when launched, 1 when this GEMM cannot take the tensor-core path
 // (unaligned operand: the caller runs the SIMT kernel), -1 on a launch error.
-template <int BN, int BK, int STAGES>
+template <int BN, int BK, int STAGES, int MH>
 inline int launch_tc_bn(const TcArgs& t, const TcWeights& w, int* err, int sm_count, cudaStream_t s) {
-  using L = TcSmem<BN, BK, STAGES>;
+  using L = TcSmem<BN, BK, STAGES, MH>;
   static bool attr_set = false;
   if (!attr_set) {
-    if (cudaFuncSetAttribute(tc_gemm_kernel<BN, BK, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    if (cudaFuncSetAttribute(tc_gemm_kernel<BN, BK, STAGES, MH>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              L::TOTAL) != cudaSuccess)
       return -1;
     attr_set = true;
   }
   CUtensorMap map_a;
-  if (!make_map_2d(&map_a, t.A, t.M, t.K, t.K, kTcBM, BK)) return 1;
+  if (!make_map_2d(&map_a, t.A, t.M, t.K, t.K, kTcBM * MH, BK)) return 1;
   TcKernelParams p;
   p.bias = t.bias;
   p.res = t.res;
@@ -587,11 +595,11 @@ inline int launch_tc_bn(const TcArgs& t, const TcWeights& w, int* err, int sm_co
   if (p.epi & EPI_BIAS_FIRST) p.epi = (p.epi & ~(uint32_t)EPI_BIAS_FIRST) | EPI_BIAS_LAST;
   if (p.head.epi & EPI_BIAS_FIRST) p.head.epi = (p.head.epi & ~(uint32_t)EPI_BIAS_FIRST) | EPI_BIAS_LAST;
   if (p.head.n > 0 && (t.N > BN || p.head.n > kTcMaxHeadN || t.N > kTcMaxHeadK)) return 1;
-  const int64_t ntiles = ((t.M + kTcBM - 1) / kTcBM) * ((t.N + BN - 1) / BN);
+  const int64_t ntiles = ((t.M + kTcBM * MH - 1) / (kTcBM * MH)) * ((t.N + BN - 1) / BN);
   const unsigned grid = (unsigned)std::min<int64_t>(ntiles, sm_count);
   const int bi = tc_bn_index(BN);
   const int ki = BK == 32 ? 0 : 1;
-  tc_gemm_kernel<BN, BK, STAGES><<<grid, kTcThreads, L::TOTAL, s>>>(map_a, w.map_hi[ki][bi], w.map_lo[ki][bi], p);
+  tc_gemm_kernel<BN, BK, STAGES, MH><<<grid, kTcThreads, L::TOTAL, s>>>(map_a, w.map_hi[ki][bi], w.map_lo[ki][bi], p);
   return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 
@@ -611,6 +619,7 @@ inline int tc_choose_bn(int64_t M, int64_t N, int sm_count, bool head) {
 struct TcConfig {
   int bn = 0;  // 64, 128 or 256
   int bk = 0;  // 16 or 32
+  int mh = 0;  // tile rows: 1 -> 128, 2 -> 256 (two M=128 MMAs share each W k-block)
 };
 
 inline int launch_tc_gemm(const TcArgs& t, const TcWeights& w, int* err, int sm_count, cudaStream_t s,
@@ -619,17 +628,24 @@ inline int launch_tc_gemm(const TcArgs& t, const TcWeights& w, int* err, int sm_
   if (t.M > 0x7fffffff / 2 || t.N > 65535 * 64) return 1;
   const int bn = cfg.bn ? cfg.bn : tc_choose_bn(t.M, t.N, sm_count, t.head.n > 0);
   const int bk = cfg.bk ? cfg.bk : 16;
+  const int mh = (cfg.mh == 2 && bn <= 128) ? 2 : 1;
+  if (mh == 2) {
+    if (bk == 32) return bn == 64 ? launch_tc_bn<64, 32, 2, 2>(t, w, err, sm_count, s)
+                                   : launch_tc_bn<128, 32, 2, 2>(t, w, err, sm_count, s);
+    return bn == 64 ? launch_tc_bn<64, 16, 4, 2>(t, w, err, sm_count, s)
+                    : launch_tc_bn<128, 16, 4, 2>(t, w, err, sm_count, s);
+  }
   if (bk == 32) {
     switch (bn) {
-      case 64: return launch_tc_bn<64, 32, 4>(t, w, err, sm_count, s);
-      case 128: return launch_tc_bn<128, 32, 3>(t, w, err, sm_count, s);
-      default: return launch_tc_bn<256, 32, 2>(t, w, err, sm_count, s);
+      case 64: return launch_tc_bn<64, 32, 4, 1>(t, w, err, sm_count, s);
+      case 128: return launch_tc_bn<128, 32, 3, 1>(t, w, err, sm_count, s);
+      default: return launch_tc_bn<256, 32, 2, 1>(t, w, err, sm_count, s);
     }
   }
   switch (bn) {
-    case 64: return launch_tc_bn<64, 16, 8>(t, w, err, sm_count, s);
-    case 128: return launch_tc_bn<128, 16, 6>(t, w, err, sm_count, s);
-    default: return launch_tc_bn<256, 16, 4>(t, w, err, sm_count, s);
+    case 64: return launch_tc_bn<64, 16, 8, 1>(t, w, err, sm_count, s);
+    case 128: return launch_tc_bn<128, 16, 6, 1>(t, w, err, sm_count, s);
+    default: return launch_tc_bn<256, 16, 4, 1>(t, w, err, sm_count, s);
   }
 }
 

@@ -121,10 +121,12 @@ FORGETUNE_EXPORT int ftb_model_create(const void* blob, size_t bytes, void** mod
 FORGETUNE_EXPORT void ftb_model_destroy(void* model);
 FORGETUNE_EXPORT int ftb_model_set_devices(void* model, const int* device_ids, int n);
 FORGETUNE_EXPORT int ftb_model_set_policy(void* model, int policy);
-/* Tensor-core tile width (0, 64, 128, 256; 0 = by shape) and k-block (0, 16,
- * 32) of launch-list step `step`, and whether a following small-N head is
- * fused into its epilogue.  For the autotuner; call between runs. */
-FORGETUNE_EXPORT int ftb_model_set_step_config(void* model, int step, int tc_bn, int tc_bk, int fuse_head);
+/* Tensor-core tile of launch-list step `step`: width tc_bn (0, 64, 128, 256),
+ * k-block tc_bk (0, 16, 32), rows tc_mh x 128 (0, 1, 2; 2 needs tc_bn <= 128);
+ * 0 = chosen by shape.  fuse_head: compute a following small-N head in the
+ * epilogue.  For the autotuner; call between runs. */
+FORGETUNE_EXPORT int ftb_model_set_step_config(void* model, int step, int tc_bn, int tc_bk, int tc_mh,
+                                               int fuse_head);
 FORGETUNE_EXPORT int ftb_model_prepare(void* model);
 /* Failure-detection hook (tests): while tc_stall != 0 every tensor-core
  * launch of the model makes one pipeline wait that nothing completes run out

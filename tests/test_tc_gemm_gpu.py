@@ -83,3 +83,37 @@ def test_fused_small_head_matches_oracle(M, K, H, N2, tmp_path):
     assert np.allclose(got, want, atol=1e-4, rtol=1e-4), float(np.max(np.abs(got - want)))
     assert np.array_equal(got.view(np.uint32), cm.run(x).view(np.uint32))
     cm.close()
+
+
+TILE_CONFIGS = [(64, 16, 1), (128, 16, 1), (256, 16, 1), (64, 32, 1), (128, 32, 1), (256, 32, 1),
+                (64, 16, 2), (128, 16, 2), (64, 32, 2), (128, 32, 2)]
+
+
+@pytest.mark.parametrize("M,K,N", [(3000, 784, 256), (700, 96, 130), (2300, 512, 64)])
+def test_every_tile_configuration_agrees(M, K, N, tmp_path):
+    """Tile width, k-block and 128/256-row tiles change only the schedule: each
+    output element is the same sequence of MMAs, so all configurations give
+    the same bits, within tolerance of the oracle."""
+    from forgetune_b200 import _native
+    torch.manual_seed(M)
+    m = Block(K, N, True, False).eval()
+    cm = compile_model(m, (torch.randn(2, K),), output_dir=str(tmp_path), autotune=False, enable_fusion=True,
+                       kernel_variant="fused_ikj", dynamic_batch=True, max_batch_size=M,
+                       gpu_kernel="tcgen05", verify=False)
+    with open(cm.manifest()["artifacts"]["graph_blob"], "rb") as f:
+        eng = _native.EngineModel(f.read())
+    eng.set_devices([torch.cuda.current_device()])
+    x = np.random.default_rng(K).standard_normal((M, K)).astype(np.float32)
+    want = oracle.gemm(x, m.fc.weight.detach().numpy().T.copy(), m.fc.bias.detach().numpy(), relu=True,
+                       order="bias_last")
+    first = None
+    for bn, bk, mh in TILE_CONFIGS:
+        eng.set_step_config(0, bn, bk, mh, True)
+        y = np.zeros((M, N), np.float32)
+        assert eng.run(x, y) == 0, _native.last_error()
+        assert np.allclose(y, want, atol=1e-4, rtol=1e-4), (bn, bk, mh, float(np.max(np.abs(y - want))))
+        if first is None:
+            first = y.copy()
+        assert np.array_equal(y.view(np.uint32), first.view(np.uint32)), (bn, bk, mh)
+    eng.close()
+    cm.close()
