@@ -30,7 +30,7 @@ _SIGS = {
     "ftb_model_set_devices": ([c_void_p, c_void_p, c_int], c_int),
     "ftb_model_set_policy": ([c_void_p, c_int], c_int),
     "ftb_model_prepare": ([c_void_p], c_int),
-    "ftb_model_set_step_config": ([c_void_p, c_int, c_int, c_int, c_int, c_int], c_int),
+    "ftb_model_set_step_config": ([c_void_p, c_int, c_int, c_int, c_int, c_int, c_int], c_int),
     "ftb_model_set_fault_injection": ([c_void_p, c_int], c_int),
     "ftb_model_run": ([c_void_p, c_void_p, c_size_t, c_void_p, c_size_t, c_int64, c_int], c_int),
     "ftb_model_run_device": ([c_void_p, c_void_p, c_size_t, c_void_p, c_size_t, c_int64, c_void_p], c_int),
@@ -136,10 +136,10 @@ class EngineModel:
     def prepare(self) -> None:
         self._check(lib().ftb_model_prepare(self.handle), "prepare")
 
-    def set_step_config(self, step: int, tc_bn: int = 0, tc_bk: int = 0, tc_mh: int = 0,
+    def set_step_config(self, step: int, tc_bn: int = 0, tc_bk: int = 0, tc_mh: int = 0, tc_pair: int = 0,
                         fuse_head: bool = True) -> None:
-        self._check(lib().ftb_model_set_step_config(self.handle, step, tc_bn, tc_bk, tc_mh, int(fuse_head)),
-                    "set_step_config")
+        self._check(lib().ftb_model_set_step_config(self.handle, step, tc_bn, tc_bk, tc_mh, tc_pair,
+                                                    int(fuse_head)), "set_step_config")
 
     def run(self, x, out, api: int = 2) -> int:
         return int(lib().ftb_model_run(self.handle, x.ctypes.data, x.size, out.ctypes.data, out.size,

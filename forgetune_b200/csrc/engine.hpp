@@ -190,6 +190,7 @@ struct Step {
   int32_t tc_bn = 0;
   int32_t tc_bk = 0;
   int32_t tc_mh = 0;  // 128-row halves per tile (0 = by shape)
+  int32_t tc_pair = 0;  // 2 = 256-row tiles on an SM pair, 1 = one SM per tile (0 = by shape)
   bool fuse_head = true;
 };
 

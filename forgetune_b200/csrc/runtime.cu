@@ -30,7 +30,7 @@
 #include "philox.cuh"
 #include "simt_gemm.cuh"
 #include "splitk_gemv.cuh"
-#include "tc_gemm.cuh"
+#include "tc_pair_gemm.cuh"
 
 #define FTB_API extern "C" __attribute__((visibility("default")))
 
@@ -554,6 +554,7 @@ static int enqueue(const Model* m, const Replica* rep, ExecCtx* c, const float* 
             cfg.bn = st.tc_bn;
             cfg.bk = st.tc_bk;
             cfg.mh = st.tc_mh;
+            cfg.pair = st.tc_pair;
             if (st.head_step >= 0 && st.fuse_head) {
               const Step& hs = rep->steps[(size_t)st.head_step];
               t.head.w = ptr(hs.b);
@@ -922,7 +923,8 @@ FTB_API int ftb_model_set_policy(void* handle, int policy) {
 // Tensor-core tile configuration of one launch-list step (0 = by shape) and
 // whether a following small-N head is fused into its epilogue.  Used by the
 // autotuner; call between runs, not concurrently with them.
-FTB_API int ftb_model_set_step_config(void* handle, int step, int tc_bn, int tc_bk, int tc_mh, int fuse_head) {
+FTB_API int ftb_model_set_step_config(void* handle, int step, int tc_bn, int tc_bk, int tc_mh, int tc_pair,
+                                      int fuse_head) {
   auto* m = static_cast<Model*>(handle);
   if (!m) return ST_NULL;
   if (step < 0 || step >= (int)m->prog.steps.size()) {
@@ -930,8 +932,12 @@ FTB_API int ftb_model_set_step_config(void* handle, int step, int tc_bn, int tc_
     return ST_CONFIG;
   }
   if (!(tc_bn == 0 || tc_bn == 64 || tc_bn == 128 || tc_bn == 256) || !(tc_bk == 0 || tc_bk == 16 || tc_bk == 32) ||
-      !(tc_mh >= 0 && tc_mh <= 2)) {
-    set_error("tile width must be 0, 64, 128 or 256, k-block 0, 16 or 32, row halves 0, 1 or 2");
+      !(tc_mh >= 0 && tc_mh <= 2) || !(tc_pair >= 0 && tc_pair <= 2)) {
+    set_error("tile width must be 0, 64, 128 or 256, k-block 0, 16 or 32, row halves 0, 1 or 2, pair 0, 1 or 2");
+    return ST_CONFIG;
+  }
+  if (tc_pair == 2 && (tc_mh == 2 || (tc_bn != 0 && tc_bn < 128))) {
+    set_error("SM-pair tiles are 256 rows by 128 or 256 columns (row halves 0 or 1)");
     return ST_CONFIG;
   }
   std::lock_guard<std::mutex> lk(m->mu);
@@ -939,6 +945,7 @@ FTB_API int ftb_model_set_step_config(void* handle, int step, int tc_bn, int tc_
     s.tc_bn = tc_bn;
     s.tc_bk = tc_bk;
     s.tc_mh = tc_mh;
+    s.tc_pair = tc_pair;
     s.fuse_head = fuse_head != 0;
   };
   apply(m->prog.steps[(size_t)step]);

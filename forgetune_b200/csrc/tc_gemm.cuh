@@ -12,17 +12,21 @@
 // 128 x BN output tiles (n fastest, so CTAs working on one row block run
 // together and share its A tile through L2).  Ten warps:
 //   warp 0      TMA producer: A (fp32), W_hi and W_lo tiles per k-block of
-//               32, 128-byte swizzled, into a STAGES-deep ring that runs
-//               continuously across tiles;
-//   warp 1      allocates two TMEM accumulators (2 x BN columns); one thread
-//               issues tcgen05.mma (kind::tf32, M=128, N=BN, K=8) three times
-//               per k-step into the accumulator of the current tile and
-//               tcgen05.commit frees each stage / publishes each tile;
+//               16 or 32, 64- or 128-byte swizzled, into a STAGES-deep ring
+//               that runs continuously across tiles;
+//   warp 1      allocates two TMEM accumulators (2 x BN columns); the warp
+//               waits, one elected lane issues tcgen05.mma (kind::tf32,
+//               M=128, N=BN, K=8) three times per k-step into the accumulator
+//               of the current tile and tcgen05.commit frees each stage /
+//               publishes each tile;
 //   warps 2-5   split each A tile in shared memory (hi in place, lo beside);
 //   warps 6-9   epilogue of the previous tile, overlapping the MMAs of the
-//               next: tcgen05.ld, a per-warp shared-memory transpose so each
-//               store instruction writes 128 contiguous bytes of one row,
-//               then bias / ReLU / residual.
+//               next: tcgen05.ld (lane = row, 32 columns), bias / ReLU /
+//               residual in registers, then a 128-byte-swizzled staging tile
+//               per warp and a TMA store (or, for output rows that are not
+//               16-byte aligned, a shared-memory transpose and row stores;
+//               or, with a fused small head, the head's dot products).
+// tc_pair_gemm.cuh runs the same roles on SM pairs (256-row tiles).
 // Every mbarrier wait is bounded: on timeout the kernel records an error
 // code, skips the remaining work, waits (bounded) for MMAs in flight,
 // releases its TMEM and returns.
@@ -31,6 +35,8 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
+#include <atomic>
 #include <cstdint>
 #include <cstring>
 
@@ -78,6 +84,7 @@ struct TcKernelParams {
   uint32_t epi;
   TcHead head;
   int* err;  // device error word: 0 ok, nonzero = a bounded wait gave up
+  int y_tma;  // the output has a TMA map (rows 16-byte aligned): TMA-store epilogue
   // test hook: the MMA thread first waits on a barrier nothing completes, so
   // the bounded wait runs out and the abort path runs (failure-detection tests)
   int stall_test;
@@ -170,6 +177,24 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   }
 }
 
+// mbar_wait by every lane of a warp, with one outcome for the whole warp.
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* err,
+                                               int code, bool ignore_abort = false) {
+  const bool ok = mbar_wait(bar, parity, abort_flag, err, code, ignore_abort);
+  return __all_sync(0xffffffffu, ok);
+}
+
+// One lane of a converged warp (elect.sync): the same lane on every call.
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred;
+  asm volatile(
+      "{\n\t.reg .pred P;\n\t.reg .b32 R;\n\t"
+      "elect.sync R|P, 0xffffffff;\n\t"
+      "selp.u32 %0, 1, 0, P;\n\t}"
+      : "=r"(pred));
+  return pred != 0;
+}
+
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int c0, int c1, uint64_t* bar) {
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
@@ -238,6 +263,268 @@ __device__ __forceinline__ float tf32_rna(float v) {
         "=r"(r[30]), "=r"(r[31])                                                                             \
       : "r"(taddr))
 
+// Split the A values of one stage into tf32 hi (in place) and lo; 128
+// threads, N4 float4 each.
+template <int N4>
+__device__ __forceinline__ void tc_split_a(float4* hi, float4* lo, int t128) {
+#pragma unroll
+  for (int i = 0; i < N4; ++i) {
+    const int idx = t128 + i * 128;
+    const float4 v = hi[idx];
+    float4 h, l;
+    h.x = tf32_rna(v.x);
+    h.y = tf32_rna(v.y);
+    h.z = tf32_rna(v.z);
+    h.w = tf32_rna(v.w);
+    l.x = tf32_rna(v.x - h.x);
+    l.y = tf32_rna(v.y - h.y);
+    l.z = tf32_rna(v.z - h.z);
+    l.w = tf32_rna(v.w - h.w);
+    hi[idx] = h;
+    lo[idx] = l;
+  }
+}
+
+// Shared-memory views of one epilogue warp.
+struct TcEpiSmem {
+  float* tr;             // this warp's 32 x 33 transpose tile
+  float* stage;          // this warp's 32 x 32 TMA-store tile (1024-byte aligned; overlaps the transpose tiles)
+  const float* head_w;   // head weights [N][hp], zero padded
+  const float* bias_a;   // bias of this GEMM as the head path reads it
+  const float* head_bb;  // bias of the head, [hp]
+  int hn, hp;            // head width, padded to whole float4s
+};
+
+// Run by the four epilogue warps (threads 192..319): stage the head weights
+// and both biases once (all four warps read them).
+// `epi` is the 1024-byte aligned epilogue area (4 x 32 x 33 floats) and
+// `w` this warp's index among the four.
+__device__ __forceinline__ TcEpiSmem tc_epi_setup(const TcKernelParams& p, float* epi, int w, float* head_smem) {
+  TcEpiSmem e;
+  e.tr = epi + w * 32 * 33;
+  e.stage = epi + w * 32 * 32;
+  e.hn = p.head.n;
+  e.hp = (e.hn + 3) & ~3;
+  float* head_w = head_smem;
+  float* head_ba = head_smem + kTcMaxHeadK * kTcMaxHeadN;  // bias of this GEMM, [N]
+  float* head_bb = head_ba + kTcMaxHeadK;                  // bias of the head, [hp]
+  e.head_w = head_w;
+  e.head_bb = head_bb;
+  e.bias_a = (p.epi & EPI_BIAS_ROWS) ? p.bias : head_ba;
+  if (e.hn > 0) {
+    const int hn = e.hn, hp = e.hp;
+    for (int i = threadIdx.x - 192; i < p.N * hp; i += 128) {
+      const int k = i / hp, o = i - k * hp;
+      head_w[i] = o < hn ? p.head.w[k * hn + o] : 0.0f;
+    }
+    for (int i = threadIdx.x - 192; i < p.N; i += 128)
+      head_ba[i] = (p.bias && !(p.epi & EPI_BIAS_ROWS)) ? p.bias[i] : 0.0f;
+    for (int i = threadIdx.x - 192; i < hp; i += 128) head_bb[i] = (p.head.bias && i < hn) ? p.head.bias[i] : 0.0f;
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+  }
+  return e;
+}
+
+// src[4 i .. 4 i + 3] of a run of 32 floats: one four-wide load when `vec`
+// (all 32 in bounds and src 16-byte aligned), else the elements below cnt
+// and zeros.
+__device__ __forceinline__ float4 ld4(const float* src, int i, bool vec, int cnt) {
+  if (vec) return reinterpret_cast<const float4*>(src)[i];
+  float4 t;
+  t.x = 4 * i + 0 < cnt ? src[4 * i + 0] : 0.0f;
+  t.y = 4 * i + 1 < cnt ? src[4 * i + 1] : 0.0f;
+  t.z = 4 * i + 2 < cnt ? src[4 * i + 2] : 0.0f;
+  t.w = 4 * i + 3 < cnt ? src[4 * i + 3] : 0.0f;
+  return t;
+}
+
+__device__ __forceinline__ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+// The epilogue of apply_epilogue on columns 4 i .. 4 i + 3 of a run of 32
+// consecutive columns of row m held by this lane: per element the same
+// operations in the same order, so the bits are the same.  bsrc points at the
+// bias of the run's first column (a column bias: the same address in every
+// lane, a broadcast; or the [M, N] bias at [m, n]), rsrc at the residual
+// [m, n]; bvec / rvec: four-wide loads allowed; cnt = columns in range.
+__device__ __forceinline__ void epi_group(float (&e)[4], uint32_t epi, const float* bsrc, bool bvec,
+                                          const float* rsrc, bool rvec, int i, int cnt) {
+  // flags as predicates: every step is a select, so the unrolled loops stay
+  // one basic block and the loads can be scheduled early
+  const bool bias = epi & EPI_BIAS_LAST, pre = epi & EPI_RELU_PRE, res = epi & EPI_RESIDUAL,
+             post = epi & EPI_RELU_POST;
+  const float4 b = bias ? ld4(bsrc, i, bvec, cnt) : make_float4(0.f, 0.f, 0.f, 0.f);
+  const float4 r = res ? ld4(rsrc, i, rvec, cnt) : make_float4(0.f, 0.f, 0.f, 0.f);
+  const float bb[4] = {b.x, b.y, b.z, b.w};
+  const float rr[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    float v = e[k];
+    v = bias ? __fadd_rn(v, bb[k]) : v;
+    v = pre ? relu_keep_nan(v) : v;
+    v = res ? __fadd_rn(v, rr[k]) : v;
+    v = post ? relu_keep_nan(v) : v;
+    e[k] = v;
+  }
+}
+
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int c0, int c1) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(c0), "r"(c1), "r"(smem_u32(src))
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+// Rows whose N <= BN hidden values stay in TMEM: lane = row m, the head's
+// outputs y2[m, o] = epi2(sum_n y[m, n] W2[n, o] + b2[o]) accumulated over n
+// in order (the reference's loop order), each y[m, n] finished by the GEMM's
+// epilogue four columns at a time and consumed at once.
+template <int HP4, bool FULL>
+__device__ __forceinline__ void head_chunk(float (&acc)[4 * HP4], const uint32_t (&r)[32], const TcKernelParams& p,
+                                           const TcEpiSmem& e, int m, int c, int cnt) {
+  const uint32_t epi = p.epi;
+  const int64_t off = (int64_t)m * p.N + c;
+  // the column bias is staged in shared memory for all 256 columns
+  const float* bsrc = (epi & EPI_BIAS_ROWS) ? p.bias + off : e.bias_a + c;
+  const bool bvec = FULL && aligned16(bsrc);
+  const bool rvec = FULL && aligned16(p.res + off);
+  const float4* w4 = reinterpret_cast<const float4*>(e.head_w) + (int64_t)c * HP4;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    float v[4] = {__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1]), __uint_as_float(r[4 * i + 2]),
+                  __uint_as_float(r[4 * i + 3])};
+    epi_group(v, epi, bsrc, bvec, p.res + off, rvec, i, FULL ? 32 : cnt);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int j = 4 * i + k;
+      if (FULL || j < cnt) {
+#pragma unroll
+        for (int o4 = 0; o4 < HP4; ++o4) {
+          const float4 w = w4[j * HP4 + o4];
+          acc[4 * o4 + 0] = fmaf(v[k], w.x, acc[4 * o4 + 0]);
+          acc[4 * o4 + 1] = fmaf(v[k], w.y, acc[4 * o4 + 1]);
+          acc[4 * o4 + 2] = fmaf(v[k], w.z, acc[4 * o4 + 2]);
+          acc[4 * o4 + 3] = fmaf(v[k], w.w, acc[4 * o4 + 3]);
+        }
+      }
+    }
+  }
+}
+
+// Rows whose N <= BN hidden values stay in TMEM: lane = row m, the head's
+// outputs y2[m, o] = epi2(sum_n y[m, n] W2[n, o] + b2[o]) accumulated over n
+// in order (the reference's loop order), each y[m, n] finished by the GEMM's
+// epilogue four columns at a time and consumed at once.
+template <int HP4>
+__device__ __forceinline__ void tc_head_rows(const TcKernelParams& p, const TcEpiSmem& e, uint32_t base, int m) {
+  float acc[4 * HP4];
+#pragma unroll
+  for (int o = 0; o < 4 * HP4; ++o) acc[o] = 0.0f;
+#pragma unroll 1
+  for (int c = 0; c < p.N; c += 32) {
+    uint32_t r[32];
+    __syncwarp();
+    FTB_TMEM_LD32(base + (uint32_t)c, r);
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+    const int cnt = min(32, p.N - c);
+    if (m < p.M) {
+      if (cnt == 32)
+        head_chunk<HP4, true>(acc, r, p, e, m, c, cnt);
+      else
+        head_chunk<HP4, false>(acc, r, p, e, m, c, cnt);
+    }
+  }
+  if (m < p.M) {
+#pragma unroll
+    for (int o = 0; o < 4 * HP4; ++o)
+      if (o < e.hn) p.head.y[(int64_t)m * e.hn + o] = apply_epilogue(acc[o], p.head.epi, e.head_bb, nullptr, m, o, e.hn);
+  }
+}
+
+// Epilogue of one 128-row accumulator block: TMEM columns [base, base + BN)
+// of this warp's lane quarter q hold rows m0 + 32 q + lane, output columns
+// n0 + c.  With a head: y stays in registers and the head's outputs are
+// stored.  Otherwise, when the output rows are 16-byte aligned (y_tma), each
+// lane finishes its row's 32 columns in registers, writes them into this
+// warp's 128-byte-swizzled staging tile and one lane stores the 32 x 32 block
+// with TMA (which clips at the matrix edges); else the block is transposed
+// through shared memory so each store instruction writes 128 contiguous bytes.
+template <int BN>
+__device__ __forceinline__ void tc_epilogue_block(const TcKernelParams& p, const CUtensorMap* map_y,
+                                                  const TcEpiSmem& e, uint32_t base, int m0, int n0, int q,
+                                                  int lane) {
+  if (e.hn > 0) {
+    const int m = m0 + q * 32 + lane;
+    switch (e.hp) {
+      case 4: tc_head_rows<1>(p, e, base, m); break;
+      case 8: tc_head_rows<2>(p, e, base, m); break;
+      case 12: tc_head_rows<3>(p, e, base, m); break;
+      default: tc_head_rows<4>(p, e, base, m); break;
+    }
+    return;
+  }
+  if (p.y_tma) {
+    float* stage = e.stage;  // 32 rows x 128 bytes, 1024-byte aligned
+    const int m = m0 + q * 32 + lane;
+    const bool row_ok = m < p.M;
+#pragma unroll 1
+    for (int c = 0; c < BN && n0 + c < p.N; c += 32) {
+      uint32_t r[32];
+      __syncwarp();
+      FTB_TMEM_LD32(base + (uint32_t)c, r);
+      asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+      const int n = n0 + c;
+      const int cnt = min(32, p.N - n);
+      const int64_t off = (int64_t)(row_ok ? m : 0) * p.N + n;
+      // rows past M load nothing of the [M, N] operands; TMA drops them
+      const uint32_t epi = row_ok ? p.epi : (p.epi & ~(uint32_t)(EPI_BIAS_ROWS | EPI_RESIDUAL));
+      const float* bsrc = (epi & EPI_BIAS_ROWS) ? p.bias + off : p.bias + n;
+      const bool bvec = cnt == 32 && aligned16(bsrc);
+      const bool rvec = cnt == 32 && aligned16(p.res + off);
+      // the previous block's store has finished reading the staging tile
+      if (lane == 0) bulk_wait_read();
+      __syncwarp();
+      float4* row = reinterpret_cast<float4*>(stage + lane * 32);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        float v[4] = {__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1]), __uint_as_float(r[4 * i + 2]),
+                      __uint_as_float(r[4 * i + 3])};
+        epi_group(v, epi, bsrc, bvec, p.res + off, rvec, i, cnt);
+        row[i ^ (lane & 7)] = make_float4(v[0], v[1], v[2], v[3]);
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        tma_store_2d(map_y, stage, n, m0 + q * 32);
+        bulk_commit();
+      }
+    }
+    return;
+  }
+  float* tr = e.tr;
+#pragma unroll 1
+  for (int c = 0; c < BN; c += 32) {
+    uint32_t r[32];
+    __syncwarp();  // tcgen05.ld is warp-collective
+    FTB_TMEM_LD32(base + (uint32_t)c, r);
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+    // lane holds row (q*32 + lane), columns c..c+31: transpose through smem
+#pragma unroll
+    for (int j = 0; j < 32; ++j) tr[lane * 33 + j] = __uint_as_float(r[j]);
+    __syncwarp();
+    const int n = n0 + c + lane;
+    if (n < p.N) {
+      const int rows = min(32, p.M - (m0 + q * 32));
+      for (int i = 0; i < rows; ++i) {
+        const int m = m0 + q * 32 + i;
+        p.Y[(int64_t)m * p.N + n] = apply_epilogue(tr[i * 33 + lane], p.epi, p.bias, p.res, m, n, p.N);
+      }
+    }
+  }
+}
+
 template <int BN, int BK, int STAGES, int MH>
 struct TcSmem {
   static constexpr int A_HALF_BYTES = kTcBM * BK * 4;  // one 128-row half of the A tile
@@ -256,7 +543,8 @@ struct TcSmem {
 template <int BN, int BK, int STAGES, int MH>
 __global__ void __launch_bounds__(kTcThreads, 1)
 tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_bhi,
-               const __grid_constant__ CUtensorMap map_blo, TcKernelParams p) {
+               const __grid_constant__ CUtensorMap map_blo, const __grid_constant__ CUtensorMap map_y,
+               TcKernelParams p) {
   using L = TcSmem<BN, BK, STAGES, MH>;
   static_assert(L::TOTAL <= 227 * 1024, "shared memory budget");
   static_assert(MH == 1 || MH == 2, "tiles of 128 or 256 rows");
@@ -317,43 +605,50 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
-    if (lane == 0) {
-      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_a)) : "memory");
-      uint32_t it = 0;
-      bool ok = true;
-      for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
-        const int m0 = (t / tiles_n) * BMT;
-        const int n0 = (t % tiles_n) * BN;
-        for (int kb = 0; kb < nk; ++kb, ++it) {
-          const int s = (int)(it % STAGES);
-          const uint32_t r = it / STAGES;
-          if (!(ok = mbar_wait(&empty[s], (r & 1u) ^ 1u, abort_flag, p.err, 1))) break;
+    // TMA producer: the whole warp runs the loop (so the loop state is
+    // warp-uniform); one elected lane issues the copies
+    if (lane == 0) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_a)) : "memory");
+    uint32_t it = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+      const int m0 = (t / tiles_n) * BMT;
+      const int n0 = (t % tiles_n) * BN;
+      for (int kb = 0; kb < nk; ++kb, ++it) {
+        const int s = (int)(it % STAGES);
+        const uint32_t r = it / STAGES;
+        if (!(ok = mbar_wait_warp(&empty[s], (r & 1u) ^ 1u, abort_flag, p.err, 1))) break;
+        if (elect_one()) {
           mbar_arrive_expect_tx(&full[s], L::TX_BYTES);
           tma_load_2d(a_tile(s), &map_a, kb * BK, m0, &full[s]);
           tma_load_2d(bhi_tile(s), &map_bhi, kb * BK, n0, &full[s]);
           tma_load_2d(blo_tile(s), &map_blo, kb * BK, n0, &full[s]);
         }
+        __syncwarp();
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
-      const uint32_t idesc = idesc_tf32<BN>();
-      uint32_t it = 0, tc = 0;
-      bool ok = true;
-      if (p.stall_test) ok = mbar_wait(never, 0, abort_flag, p.err, 9);
-      for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x, ++tc) {
-        const uint32_t buf = tc & 1u, use = tc >> 1;
-        if (!(ok = mbar_wait(&acce[buf], (use & 1u) ^ 1u, abort_flag, p.err, 2))) break;
+    // MMA issuer: the whole warp waits and computes descriptors; one elected
+    // lane issues the MMAs and the commits that track them.  It waits only
+    // for the converters: they arrive after waiting for the whole stage
+    // (A and both W halves) to land, so their arrival orders the W copies
+    // before the MMAs too.
+    const uint32_t idesc = idesc_tf32<BN>();
+    uint32_t it = 0, tc = 0;
+    bool ok = true;
+    if (p.stall_test) ok = mbar_wait_warp(never, 0, abort_flag, p.err, 9);
+    for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x, ++tc) {
+      const uint32_t buf = tc & 1u, use = tc >> 1;
+      if (!(ok = mbar_wait_warp(&acce[buf], (use & 1u) ^ 1u, abort_flag, p.err, 2))) break;
+      tc_fence_after();
+      const uint32_t d = tmem + buf * (uint32_t)(MH * BN);
+      for (int kb = 0; kb < nk; ++kb, ++it) {
+        const int s = (int)(it % STAGES);
+        const uint32_t par = (it / STAGES) & 1u;
+        if (!(ok = mbar_wait_warp(&conv[s], par, abort_flag, p.err, 4))) break;
         tc_fence_after();
-        const uint32_t d = tmem + buf * (uint32_t)(MH * BN);
-        for (int kb = 0; kb < nk; ++kb, ++it) {
-          const int s = (int)(it % STAGES);
-          const uint32_t par = (it / STAGES) & 1u;
-          ok = mbar_wait(&full[s], par, abort_flag, p.err, 3) && mbar_wait(&conv[s], par, abort_flag, p.err, 4);
-          if (!ok) break;
-          tc_fence_after();
-          const uint32_t ahi = smem_u32(a_tile(s)), alo = smem_u32(alo_tile(s));
-          const uint32_t bhi = smem_u32(bhi_tile(s)), blo = smem_u32(blo_tile(s));
+        const uint32_t ahi = smem_u32(a_tile(s)), alo = smem_u32(alo_tile(s));
+        const uint32_t bhi = smem_u32(bhi_tile(s)), blo = smem_u32(blo_tile(s));
+        if (elect_one()) {
 #pragma unroll
           for (int j = 0; j < BK / 8; ++j) {  // K = 8 tf32 (32 bytes) per MMA
             const uint32_t off = (uint32_t)j * 32u;
@@ -370,14 +665,19 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
           }
           umma_commit(&empty[s]);
         }
-        if (ok) umma_commit(&accf[buf]);
+        __syncwarp();
       }
-      if (!ok) {
-        // every MMA issued so far retires before this arrives; wait for it
-        // even though the CTA is aborting, so TMEM is not freed under them
-        umma_commit(drain);
-        mbar_wait(drain, 0, abort_flag, p.err, 5, /*ignore_abort=*/true);
+      if (ok) {
+        if (elect_one()) umma_commit(&accf[buf]);
+        __syncwarp();
       }
+    }
+    if (!ok) {
+      // every MMA issued so far retires before this arrives; wait for it
+      // even though the CTA is aborting, so TMEM is not freed under them
+      if (elect_one()) umma_commit(drain);
+      __syncwarp();
+      mbar_wait_warp(drain, 0, abort_flag, p.err, 5, /*ignore_abort=*/true);
     }
   } else if (warp < 6) {
     // warps 2..5: split A into tf32 hi (in place) and lo
@@ -387,25 +687,9 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
     for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
       for (int kb = 0; kb < nk; ++kb, ++it) {
         const int s = (int)(it % STAGES);
-        if (!(ok = mbar_wait(&full[s], (it / STAGES) & 1u, abort_flag, p.err, 6))) break;
-        float4* hi = reinterpret_cast<float4*>(a_tile(s));
-        float4* lo = reinterpret_cast<float4*>(alo_tile(s));
-#pragma unroll
-        for (int i = 0; i < (BMT * BK / 4) / 128; ++i) {
-          const int idx = t128 + i * 128;
-          const float4 v = hi[idx];
-          float4 h, l;
-          h.x = tf32_rna(v.x);
-          h.y = tf32_rna(v.y);
-          h.z = tf32_rna(v.z);
-          h.w = tf32_rna(v.w);
-          l.x = tf32_rna(v.x - h.x);
-          l.y = tf32_rna(v.y - h.y);
-          l.z = tf32_rna(v.z - h.z);
-          l.w = tf32_rna(v.w - h.w);
-          hi[idx] = h;
-          lo[idx] = l;
-        }
+        if (!(ok = mbar_wait_warp(&full[s], (it / STAGES) & 1u, abort_flag, p.err, 6))) break;
+        tc_split_a<(BMT * BK / 4) / 128>(reinterpret_cast<float4*>(a_tile(s)), reinterpret_cast<float4*>(alo_tile(s)),
+                                         t128);
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(&conv[s]);
@@ -414,98 +698,24 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
   } else {
     // warps 6..9: epilogue, one TMEM lane quarter each
     const int q = warp & 3;
-    float* tr = epi_stage + (warp - 6) * 32 * 33;
-    const int hn = p.head.n;
-    const int hp = (hn + 3) & ~3;  // head width padded to whole float4s
-    float* head_w = head_smem;                       // [N][hp], zero padded
-    float* head_ba = head_smem + kTcMaxHeadK * kTcMaxHeadN;  // bias of this GEMM, [N]
-    float* head_bb = head_ba + kTcMaxHeadK;                  // bias of the head, [hp]
-    const float* bias_a = (p.epi & EPI_BIAS_ROWS) ? p.bias : head_ba;
-    if (hn > 0) {
-      // stage the head weights and both biases once; all four epilogue warps read them
-      for (int i = threadIdx.x - 192; i < p.N * hp; i += 128) {
-        const int k = i / hp, o = i - k * hp;
-        head_w[i] = o < hn ? p.head.w[k * hn + o] : 0.0f;
-      }
-      for (int i = threadIdx.x - 192; i < p.N; i += 128)
-        head_ba[i] = (p.bias && !(p.epi & EPI_BIAS_ROWS)) ? p.bias[i] : 0.0f;
-      for (int i = threadIdx.x - 192; i < hp; i += 128) head_bb[i] = (p.head.bias && i < hn) ? p.head.bias[i] : 0.0f;
-      asm volatile("bar.sync 1, 128;" ::: "memory");
-    }
+    const TcEpiSmem e = tc_epi_setup(p, epi_stage, warp - 6, head_smem);
     uint32_t tc = 0;
     for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++tc) {
       const uint32_t buf = tc & 1u, use = tc >> 1;
-      if (!mbar_wait(&accf[buf], use & 1u, abort_flag, p.err, 7)) break;
+      if (!mbar_wait_warp(&accf[buf], use & 1u, abort_flag, p.err, 7)) break;
       tc_fence_after();
       const int n0 = (t % tiles_n) * BN;
 #pragma unroll 1
       for (int h = 0; h < MH; ++h) {
-      const int m0 = (t / tiles_n) * BMT + h * kTcBM;
-      const uint32_t base = tmem + (buf * MH + h) * (uint32_t)BN + ((uint32_t)(q * 32) << 16);
-      if (hn > 0) {
-        // the tile holds whole rows (N <= BN): lane = row, accumulate the head
-        const int m = m0 + q * 32 + lane;
-        float acc[kTcMaxHeadN];
-#pragma unroll
-        for (int o = 0; o < kTcMaxHeadN; ++o) acc[o] = 0.0f;
-#pragma unroll 1
-        for (int c = 0; c < p.N; c += 32) {
-          uint32_t r[32];
-          __syncwarp();
-          FTB_TMEM_LD32(base + (uint32_t)c, r);
-          asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-          if (m < p.M) {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              if (c + j < p.N) {  // warp-uniform
-                const float v = apply_epilogue(__uint_as_float(r[j]), p.epi, bias_a, p.res, m, c + j, p.N);
-                const float4* w4 = reinterpret_cast<const float4*>(head_w + (c + j) * hp);
-#pragma unroll
-                for (int o4 = 0; o4 < kTcMaxHeadN / 4; ++o4) {
-                  if (o4 * 4 < hn) {  // warp-uniform
-                    const float4 w = w4[o4];
-                    acc[4 * o4 + 0] = fmaf(v, w.x, acc[4 * o4 + 0]);
-                    acc[4 * o4 + 1] = fmaf(v, w.y, acc[4 * o4 + 1]);
-                    acc[4 * o4 + 2] = fmaf(v, w.z, acc[4 * o4 + 2]);
-                    acc[4 * o4 + 3] = fmaf(v, w.w, acc[4 * o4 + 3]);
-                  }
-                }
-              }
-            }
-          }
-        }
-        if (m < p.M) {
-#pragma unroll
-          for (int o = 0; o < kTcMaxHeadN; ++o)
-            if (o < hn)
-              p.head.y[(int64_t)m * hn + o] = apply_epilogue(acc[o], p.head.epi, head_bb, nullptr, m, o, hn);
-        }
-        continue;
+        const int m0 = (t / tiles_n) * BMT + h * kTcBM;
+        tc_epilogue_block<BN>(p, &map_y, e, tmem + (buf * MH + h) * (uint32_t)BN + ((uint32_t)(q * 32) << 16), m0,
+                              n0, q, lane);
       }
-#pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
-        uint32_t r[32];
-        __syncwarp();  // tcgen05.ld is warp-collective
-        FTB_TMEM_LD32(base + (uint32_t)c, r);
-        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-        // lane holds row (q*32 + lane), columns c..c+31: transpose through smem
-#pragma unroll
-        for (int j = 0; j < 32; ++j) tr[lane * 33 + j] = __uint_as_float(r[j]);
-        __syncwarp();
-        const int n = n0 + c + lane;
-        if (n < p.N) {
-          const int rows = min(32, p.M - (m0 + q * 32));
-          for (int i = 0; i < rows; ++i) {
-            const int m = m0 + q * 32 + i;
-            p.Y[(int64_t)m * p.N + n] = apply_epilogue(tr[i * 33 + lane], p.epi, p.bias, p.res, m, n, p.N);
-          }
-        }
-      }
-      }  // halves
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acce[buf]);
     }
+    if (lane == 0) bulk_wait_all();  // this warp's output stores are complete before the CTA leaves
   }
   tc_fence_before();
   __syncthreads();
@@ -571,12 +781,14 @@ inline bool tc_prepare_weights(TcWeights& w, int64_t N) {
 template <int BN, int BK, int STAGES, int MH>
 inline int launch_tc_bn(const TcArgs& t, const TcWeights& w, int* err, int sm_count, cudaStream_t s) {
   using L = TcSmem<BN, BK, STAGES, MH>;
-  static bool attr_set = false;
-  if (!attr_set) {
+  static std::atomic<uint64_t> attr_set{0};  // one bit per device
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -1;
+  if (!(attr_set.load() & (1ull << dev))) {
     if (cudaFuncSetAttribute(tc_gemm_kernel<BN, BK, STAGES, MH>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              L::TOTAL) != cudaSuccess)
       return -1;
-    attr_set = true;
+    attr_set.fetch_or(1ull << dev);
   }
   CUtensorMap map_a;
   if (!make_map_2d(&map_a, t.A, t.M, t.K, t.K, kTcBM * MH, BK)) return 1;
@@ -591,6 +803,11 @@ inline int launch_tc_bn(const TcArgs& t, const TcWeights& w, int* err, int sm_co
   p.head = t.head;
   p.err = err;
   p.stall_test = t.stall_test;
+  // TMA-store epilogue when the output rows are 16-byte aligned (no head:
+  // then only the head's small outputs are written)
+  CUtensorMap map_y;
+  std::memset(&map_y, 0, sizeof(map_y));
+  p.y_tma = (t.head.n == 0 && make_map_2d(&map_y, t.Y, t.M, t.N, t.N, 32, 32)) ? 1 : 0;
   // the accumulator starts at zero: a bias-first epilogue adds the bias at the end
   if (p.epi & EPI_BIAS_FIRST) p.epi = (p.epi & ~(uint32_t)EPI_BIAS_FIRST) | EPI_BIAS_LAST;
   if (p.head.epi & EPI_BIAS_FIRST) p.head.epi = (p.head.epi & ~(uint32_t)EPI_BIAS_FIRST) | EPI_BIAS_LAST;
@@ -599,7 +816,8 @@ inline int launch_tc_bn(const TcArgs& t, const TcWeights& w, int* err, int sm_co
   const unsigned grid = (unsigned)std::min<int64_t>(ntiles, sm_count);
   const int bi = tc_bn_index(BN);
   const int ki = BK == 32 ? 0 : 1;
-  tc_gemm_kernel<BN, BK, STAGES, MH><<<grid, kTcThreads, L::TOTAL, s>>>(map_a, w.map_hi[ki][bi], w.map_lo[ki][bi], p);
+  tc_gemm_kernel<BN, BK, STAGES, MH><<<grid, kTcThreads, L::TOTAL, s>>>(map_a, w.map_hi[ki][bi], w.map_lo[ki][bi],
+                                                                         map_y, p);
   return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 
@@ -611,42 +829,6 @@ inline int tc_choose_bn(int64_t M, int64_t N, int sm_count, bool head) {
   // a fused head needs whole rows in one tile; otherwise 256-wide tiles
   // halve the re-reads of A for layers whose width is a multiple of 256
   return (head || N % 256 == 0) ? 256 : 128;
-}
-
-// Tile configuration of one tensor-core launch: tile width BN and k-block BK.
-// 0 picks by shape.  Stages fill the shared memory: k-blocks of 16 (64-byte
-// swizzle) give twice the stages of 32.
-struct TcConfig {
-  int bn = 0;  // 64, 128 or 256
-  int bk = 0;  // 16 or 32
-  int mh = 0;  // tile rows: 1 -> 128, 2 -> 256 (two M=128 MMAs share each W k-block)
-};
-
-inline int launch_tc_gemm(const TcArgs& t, const TcWeights& w, int* err, int sm_count, cudaStream_t s,
-                          TcConfig cfg = TcConfig{}) {
-  if (!w.maps_ready || t.M <= 0) return 1;
-  if (t.M > 0x7fffffff / 2 || t.N > 65535 * 64) return 1;
-  const int bn = cfg.bn ? cfg.bn : tc_choose_bn(t.M, t.N, sm_count, t.head.n > 0);
-  const int bk = cfg.bk ? cfg.bk : 16;
-  const int mh = (cfg.mh == 2 && bn <= 128) ? 2 : 1;
-  if (mh == 2) {
-    if (bk == 32) return bn == 64 ? launch_tc_bn<64, 32, 2, 2>(t, w, err, sm_count, s)
-                                   : launch_tc_bn<128, 32, 2, 2>(t, w, err, sm_count, s);
-    return bn == 64 ? launch_tc_bn<64, 16, 4, 2>(t, w, err, sm_count, s)
-                    : launch_tc_bn<128, 16, 4, 2>(t, w, err, sm_count, s);
-  }
-  if (bk == 32) {
-    switch (bn) {
-      case 64: return launch_tc_bn<64, 32, 4, 1>(t, w, err, sm_count, s);
-      case 128: return launch_tc_bn<128, 32, 3, 1>(t, w, err, sm_count, s);
-      default: return launch_tc_bn<256, 32, 2, 1>(t, w, err, sm_count, s);
-    }
-  }
-  switch (bn) {
-    case 64: return launch_tc_bn<64, 16, 8, 1>(t, w, err, sm_count, s);
-    case 128: return launch_tc_bn<128, 16, 6, 1>(t, w, err, sm_count, s);
-    default: return launch_tc_bn<256, 16, 4, 1>(t, w, err, sm_count, s);
-  }
 }
 
 }  // namespace ftb

@@ -1,6 +1,7 @@
 """Failure detection without a GPU fault.
 
-The tensor-core kernel bounds every mbarrier wait.  A test hook makes the MMA
+The tensor-core kernels (one SM or an SM pair per tile) bound every mbarrier
+wait.  A test hook makes the MMA
 thread wait on a barrier that nothing completes: the wait runs out (~2 s), the
 kernel raises its abort flag, drains, frees its TMEM and returns; the host
 reads the mapped error word and the run returns -5 with a message.  The same
@@ -19,7 +20,10 @@ from oracle import oracle
 pytestmark = pytest.mark.gpu
 
 
-def test_tensor_core_wait_timeout_is_reported_and_recoverable(tmp_path):
+@pytest.mark.parametrize("pair", [1, 2])
+def test_tensor_core_wait_timeout_is_reported_and_recoverable(pair, tmp_path):
+    """pair=2 runs the SM-pair kernel: the leader CTA's wait runs out, it
+    raises its peer's abort flag too, and both CTAs leave together."""
     torch.manual_seed(3)
     m = nn.Sequential(nn.Linear(256, 128), nn.ReLU()).eval()
     cm = compile_model(m, (torch.randn(2, 256),), output_dir=str(tmp_path), autotune=False, enable_fusion=True,
@@ -28,6 +32,7 @@ def test_tensor_core_wait_timeout_is_reported_and_recoverable(tmp_path):
     with open(cm.manifest()["artifacts"]["graph_blob"], "rb") as f:
         eng = _native.EngineModel(f.read())
     eng.set_devices([torch.cuda.current_device()])
+    eng.set_step_config(0, 0, 0, 0, pair, True)
     x = np.random.default_rng(0).standard_normal((2048, 256)).astype(np.float32)
     y = np.zeros((2048, 128), np.float32)
     assert eng.run(x, y) == 0

@@ -85,15 +85,18 @@ def test_fused_small_head_matches_oracle(M, K, H, N2, tmp_path):
     cm.close()
 
 
-TILE_CONFIGS = [(64, 16, 1), (128, 16, 1), (256, 16, 1), (64, 32, 1), (128, 32, 1), (256, 32, 1),
-                (64, 16, 2), (128, 16, 2), (64, 32, 2), (128, 32, 2)]
+# (tile width, k-block, 128-row halves on one SM, 2 = 256-row tiles on an SM pair)
+TILE_CONFIGS = [(64, 16, 1, 1), (128, 16, 1, 1), (256, 16, 1, 1), (64, 32, 1, 1), (128, 32, 1, 1), (256, 32, 1, 1),
+                (64, 16, 2, 1), (128, 16, 2, 1), (64, 32, 2, 1), (128, 32, 2, 1),
+                (128, 16, 1, 2), (256, 16, 1, 2), (128, 32, 1, 2), (256, 32, 1, 2)]
 
 
-@pytest.mark.parametrize("M,K,N", [(3000, 784, 256), (700, 96, 130), (2300, 512, 64)])
+@pytest.mark.parametrize("M,K,N", [(3000, 784, 256), (700, 96, 130), (2300, 512, 64), (129, 64, 300)])
 def test_every_tile_configuration_agrees(M, K, N, tmp_path):
-    """Tile width, k-block and 128/256-row tiles change only the schedule: each
-    output element is the same sequence of MMAs, so all configurations give
-    the same bits, within tolerance of the oracle."""
+    """Tile width, k-block, 128/256-row tiles and one SM or an SM pair per
+    tile change only the schedule: each output element is the same sequence
+    of MMAs, so all configurations give the same bits, within tolerance of
+    the oracle."""
     from forgetune_b200 import _native
     torch.manual_seed(M)
     m = Block(K, N, True, False).eval()
@@ -107,13 +110,40 @@ def test_every_tile_configuration_agrees(M, K, N, tmp_path):
     want = oracle.gemm(x, m.fc.weight.detach().numpy().T.copy(), m.fc.bias.detach().numpy(), relu=True,
                        order="bias_last")
     first = None
-    for bn, bk, mh in TILE_CONFIGS:
-        eng.set_step_config(0, bn, bk, mh, True)
+    for bn, bk, mh, pair in TILE_CONFIGS:
+        eng.set_step_config(0, bn, bk, mh, pair, True)
         y = np.zeros((M, N), np.float32)
         assert eng.run(x, y) == 0, _native.last_error()
-        assert np.allclose(y, want, atol=1e-4, rtol=1e-4), (bn, bk, mh, float(np.max(np.abs(y - want))))
+        assert np.allclose(y, want, atol=1e-4, rtol=1e-4), (bn, bk, mh, pair, float(np.max(np.abs(y - want))))
         if first is None:
             first = y.copy()
-        assert np.array_equal(y.view(np.uint32), first.view(np.uint32)), (bn, bk, mh)
+        assert np.array_equal(y.view(np.uint32), first.view(np.uint32)), (bn, bk, mh, pair)
+    eng.close()
+    cm.close()
+
+
+@pytest.mark.parametrize("M,K,H,N2", [(3000, 96, 128, 7), (65536, 256, 128, 10), (1500, 64, 256, 16)])
+def test_fused_head_on_sm_pairs_agrees(M, K, H, N2, tmp_path):
+    """The small head fused into the epilogue of SM-pair tiles gives the
+    same bits as on one-SM tiles."""
+    from forgetune_b200 import _native
+    torch.manual_seed(M + H)
+    m = nn.Sequential(nn.Linear(K, H), nn.ReLU(), nn.Linear(H, N2)).eval()
+    cm = compile_model(m, (torch.randn(2, K),), output_dir=str(tmp_path), autotune=False, enable_fusion=True,
+                       kernel_variant="fused_ikj", dynamic_batch=True, max_batch_size=M,
+                       max_workspace_bytes=8 << 30, gpu_kernel="tcgen05", verify=False)
+    with open(cm.manifest()["artifacts"]["graph_blob"], "rb") as f:
+        eng = _native.EngineModel(f.read())
+    eng.set_devices([torch.cuda.current_device()])
+    x = np.random.default_rng(H).standard_normal((M, K)).astype(np.float32)
+    want = oracle.run_model(m, x, "naive_ijk")
+    outs = []
+    for pair in (1, 2):
+        eng.set_step_config(0, 0, 0, 0, pair, True)
+        y = np.zeros((M, N2), np.float32)
+        assert eng.run(x, y) == 0, _native.last_error()
+        assert np.allclose(y, want, atol=1e-4, rtol=1e-4), (pair, float(np.max(np.abs(y - want))))
+        outs.append(y)
+    assert np.array_equal(outs[0].view(np.uint32), outs[1].view(np.uint32))
     eng.close()
     cm.close()
