@@ -278,15 +278,17 @@ def run_ours(args) -> int:
     flops = 2.0 * B * ds["K"] * ds["N"]
     achieved_tflops = flops / (avg[dom] / 1000.0) / 1e12
     tc_peak = peaks["bf16_tflops"] / 6.0  # 3xTF32: three tf32 MMAs at half the bf16 rate
-    traffic = None
+    traffic, kname = None, ds.get("kernel", "")
     tpath = os.path.join(HERE, "profiles", "traffic.json")
     if os.path.isfile(tpath):
         with open(tpath) as f:
-            traffic = json.load(f).get(WORKLOAD, {}).get("dominant_kernel_bytes_per_launch")
+            rec = json.load(f).get(WORKLOAD, {})
+        traffic = rec.get("dominant_kernel_bytes_per_launch")
+        kname = kname or rec.get("dominant_kernel", "")
     roofline = {
         "bound": "tensor", "achieved": achieved_tflops, "peak": tc_peak, "unit": "TFLOP/s",
         "frac": achieved_tflops / tc_peak, "traffic": traffic,
-        "kernel": "step %d: GEMM K=%d N=%d M=%d (%s)" % (dom, ds["K"], ds["N"], B, ds.get("kernel", "")),
+        "kernel": "step %d: GEMM K=%d N=%d M=%d (%s)" % (dom, ds["K"], ds["N"], B, kname),
         "algorithmic_flops_per_launch": flops, "avg_launch_ms": float(avg[dom]),
         "share_of_forward": float(avg[dom] / avg.sum()),
         "peak_basis": "fp32-accurate contraction on tensor cores = 3xTF32 = %s bf16 dense / 6 (%.0f / 6)"
