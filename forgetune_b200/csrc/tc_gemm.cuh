@@ -85,6 +85,9 @@ struct TcKernelParams {
   TcHead head;
   int* err;  // device error word: 0 ok, nonzero = a bounded wait gave up
   int y_tma;  // the output has a TMA map (rows 16-byte aligned): TMA-store epilogue
+  // SM-pair kernel: tiles from split_from on run as `split` column slices
+  int split;
+  int split_from;
   // test hook: the MMA thread first waits on a barrier nothing completes, so
   // the bounded wait runs out and the abort path runs (failure-detection tests)
   int stall_test;
@@ -453,8 +456,8 @@ __device__ __forceinline__ void tc_head_rows(const TcKernelParams& p, const TcEp
 // through shared memory so each store instruction writes 128 contiguous bytes.
 template <int BN>
 __device__ __forceinline__ void tc_epilogue_block(const TcKernelParams& p, const CUtensorMap* map_y,
-                                                  const TcEpiSmem& e, uint32_t base, int m0, int n0, int q,
-                                                  int lane) {
+                                                  const TcEpiSmem& e, uint32_t base, int m0, int n0, int width,
+                                                  int q, int lane) {
   if (e.hn > 0) {
     const int m = m0 + q * 32 + lane;
     switch (e.hp) {
@@ -470,7 +473,7 @@ __device__ __forceinline__ void tc_epilogue_block(const TcKernelParams& p, const
     const int m = m0 + q * 32 + lane;
     const bool row_ok = m < p.M;
 #pragma unroll 1
-    for (int c = 0; c < BN && n0 + c < p.N; c += 32) {
+    for (int c = 0; c < width && n0 + c < p.N; c += 32) {
       uint32_t r[32];
       __syncwarp();
       FTB_TMEM_LD32(base + (uint32_t)c, r);
@@ -505,7 +508,7 @@ __device__ __forceinline__ void tc_epilogue_block(const TcKernelParams& p, const
   }
   float* tr = e.tr;
 #pragma unroll 1
-  for (int c = 0; c < BN; c += 32) {
+  for (int c = 0; c < width; c += 32) {
     uint32_t r[32];
     __syncwarp();  // tcgen05.ld is warp-collective
     FTB_TMEM_LD32(base + (uint32_t)c, r);
@@ -709,7 +712,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
       for (int h = 0; h < MH; ++h) {
         const int m0 = (t / tiles_n) * BMT + h * kTcBM;
         tc_epilogue_block<BN>(p, &map_y, e, tmem + (buf * MH + h) * (uint32_t)BN + ((uint32_t)(q * 32) << 16), m0,
-                              n0, q, lane);
+                              n0, BN, q, lane);
       }
       tc_fence_before();
       __syncwarp();
@@ -803,6 +806,8 @@ inline int launch_tc_bn(const TcArgs& t, const TcWeights& w, int* err, int sm_co
   p.head = t.head;
   p.err = err;
   p.stall_test = t.stall_test;
+  p.split = 1;
+  p.split_from = 0;
   // TMA-store epilogue when the output rows are 16-byte aligned (no head:
   // then only the head's small outputs are written)
   CUtensorMap map_y;

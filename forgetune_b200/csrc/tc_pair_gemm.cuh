@@ -119,11 +119,33 @@ __device__ __forceinline__ void umma2_commit(uint32_t caddr) {
                : "memory");
 }
 
-// Instruction descriptor: D f32, A/B tf32, both K-major, M=256, N=BN.
-template <int BN>
-__device__ __forceinline__ uint32_t idesc_tf32_pair() {
-  return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(256 >> 4) << 24);
+// Instruction descriptor: D f32, A/B tf32, both K-major, M=256, N=n (a
+// multiple of 16, at most 256).
+__device__ __forceinline__ uint32_t idesc_tf32_pair(int n) {
+  return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(256 >> 4) << 24);
 }
+
+// The pair's list of work units.  Tiles (256 x BN) run in rounds of
+// `npairs`; when the last round is partial, its tiles are cut into `split`
+// column slices of BN / split so that more pairs share it (a slice is the
+// same MMAs on fewer columns: the results do not change).
+struct PairWork {
+  int tiles_n;  // tiles per row block
+  int full;     // units [0, full) are whole tiles, tile = unit
+  int split;    // the tiles from `full` on are cut into this many slices
+  int units;
+  __device__ __forceinline__ void unit(int u, int bn, int& m0, int& n0, int& width) const {
+    int tile = u, part = 0;
+    width = bn;
+    if (u >= full) {
+      tile = full + (u - full) / split;
+      part = (u - full) % split;
+      width = bn / split;
+    }
+    m0 = (tile / tiles_n) * 256;
+    n0 = (tile % tiles_n) * bn + part * width;
+  }
+};
 
 template <int BN, int BK, int STAGES>
 struct TcPairSmem {
@@ -175,6 +197,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
   const int tiles_m = (p.M + 255) / 256;
   const int tiles_n = (p.N + BN - 1) / BN;
   const int ntiles = tiles_m * tiles_n;
+  PairWork work;
+  work.tiles_n = tiles_n;
+  work.split = p.split > 1 ? p.split : 1;
+  work.full = work.split > 1 ? p.split_from : ntiles;
+  work.units = work.full + (ntiles - work.full) * work.split;
   const int nk = (p.K + BK - 1) / BK;
   const int pair = (int)cluster_index();
   const int npairs = (int)cluster_count();
@@ -211,9 +238,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
     if (lane == 0) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_a)) : "memory");
     uint32_t it = 0;
     bool ok = true;
-    for (int t = pair; t < ntiles && ok; t += npairs) {
-      const int m0 = (t / tiles_n) * 256 + (int)rank * kTcBM;
-      const int nb = (t % tiles_n) * BN + (int)rank * (BN / 2);
+    for (int u = pair; u < work.units && ok; u += npairs) {
+      int m0, n0, width;
+      work.unit(u, BN, m0, n0, width);
+      m0 += (int)rank * kTcBM;
+      // this CTA's half of the unit's W^T rows (a narrower slice loads the
+      // full BN/2-row box; the MMA reads only its first width/2 rows)
+      const int nb = n0 + (int)rank * (width / 2);
       for (int kb = 0; kb < nk; ++kb, ++it) {
         const int s = (int)(it % STAGES);
         const uint32_t r = it / STAGES;
@@ -229,11 +260,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
     }
   } else if (warp == 1) {
     if (rank == 0) {
-      const uint32_t idesc = idesc_tf32_pair<BN>();
       uint32_t it = 0, tc = 0;
       bool ok = true;
       if (p.stall_test) ok = pair_wait_warp(never, 0, abort_flag, peer_abort, p.err, 9);
-      for (int t = pair; t < ntiles && ok; t += npairs, ++tc) {
+      for (int u = pair; u < work.units && ok; u += npairs, ++tc) {
+        int m0, n0, width;
+        work.unit(u, BN, m0, n0, width);
+        const uint32_t idesc = idesc_tf32_pair(width);
         const uint32_t buf = tc & 1u, use = tc >> 1;
         if (!(ok = pair_wait_warp(&acce[buf], (use & 1u) ^ 1u, abort_flag, peer_abort, p.err, 2))) break;
         tc_fence_after();
@@ -284,7 +317,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
     const int t128 = threadIdx.x - 64;
     uint32_t it = 0;
     bool ok = true;
-    for (int t = pair; t < ntiles && ok; t += npairs) {
+    for (int u = pair; u < work.units && ok; u += npairs) {
       for (int kb = 0; kb < nk; ++kb, ++it) {
         const int s = (int)(it % STAGES);
         if (!(ok = pair_wait_warp(&full[s], (it / STAGES) & 1u, abort_flag, peer_abort, p.err, 6))) break;
@@ -300,13 +333,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
     const int q = warp & 3;
     const TcEpiSmem e = tc_epi_setup(p, epi_stage, warp - 6, head_smem);
     uint32_t tc = 0;
-    for (int t = pair; t < ntiles; t += npairs, ++tc) {
+    for (int u = pair; u < work.units; u += npairs, ++tc) {
       const uint32_t buf = tc & 1u, use = tc >> 1;
       if (!pair_wait_warp(&accf[buf], use & 1u, abort_flag, peer_abort, p.err, 7)) break;
       tc_fence_after();
-      const int m0 = (t / tiles_n) * 256 + (int)rank * kTcBM;
-      const int n0 = (t % tiles_n) * BN;
-      tc_epilogue_block<BN>(p, &map_y, e, tmem + buf * (uint32_t)BN + ((uint32_t)(q * 32) << 16), m0, n0, q, lane);
+      int m0, n0, width;
+      work.unit(u, BN, m0, n0, width);
+      m0 += (int)rank * kTcBM;
+      tc_epilogue_block<BN>(p, &map_y, e, tmem + buf * (uint32_t)BN + ((uint32_t)(q * 32) << 16), m0, n0, width, q,
+                            lane);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(cluster_addr(&acce[buf], 0));
@@ -377,7 +412,22 @@ inline int launch_tc_pair_bn(const TcArgs& t, const TcWeights& w, int* err, cuda
   if (p.head.epi & EPI_BIAS_FIRST) p.head.epi = (p.head.epi & ~(uint32_t)EPI_BIAS_FIRST) | EPI_BIAS_LAST;
   if (p.head.n > 0 && (t.N > BN || p.head.n > kTcMaxHeadN || t.N > kTcMaxHeadK)) return 1;
   const int64_t ntiles = ((t.M + 255) / 256) * ((t.N + BN - 1) / BN);
-  const unsigned pairs = (unsigned)std::min<int64_t>(ntiles, max_pairs);
+  // the last, partial round of tiles: cut into the slice count (1, 2 or 4,
+  // slices at least 32 columns wide) that ends it soonest; not with a fused
+  // head, which needs whole rows
+  const int64_t rem = ntiles % max_pairs;
+  int split = 1;
+  if (rem > 0 && p.head.n == 0) {
+    double best = 1.0;
+    for (int f = 2; f <= 4 && BN / f >= 32; f *= 2) {
+      const double rounds = (double)((f * rem + max_pairs - 1) / max_pairs) / f;
+      if (rounds < best) best = rounds, split = f;
+    }
+  }
+  p.split = split;
+  p.split_from = (int)(ntiles - (split > 1 ? rem : 0));
+  const int64_t units = p.split_from + (ntiles - p.split_from) * split;
+  const unsigned pairs = (unsigned)std::min<int64_t>(units, max_pairs);
   // W^T maps with boxes of BN/2 rows: each CTA loads its half
   const int bi = tc_bn_index(BN / 2);
   const int ki = BK == 32 ? 0 : 1;
