@@ -45,6 +45,8 @@ _SIGS = {
     "ftb_model_inject_alloc": ([c_void_p], None),
     "ftb_model_describe": ([c_void_p, c_void_p, c_size_t], c_int),
     "ftb_device_count": ([], c_int),
+    "ftb_device_info": ([c_int, c_void_p, c_size_t], c_int),
+    "ftb_model_set_tuning": ([c_void_p, c_void_p, c_int], c_int),
     "ftb_philox_normal": ([c_void_p, c_uint64, c_uint64, c_uint64, c_void_p], c_int),
     "ftb_small_gemm_noalloc": ([c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64,
                                 ctypes.c_uint32, c_void_p], c_int),
@@ -94,6 +96,17 @@ def device_count() -> int:
     return int(lib().ftb_device_count())
 
 
+def device_info(device: int = 0) -> dict:
+    """Name, compute capability, SM count, memory and driver / runtime versions of a CUDA device."""
+    L = lib()
+    n = L.ftb_device_info(device, None, 0)
+    if n < 0:
+        raise ForgeTuneRuntimeError("ftb_device_info failed (%d): %s" % (n, last_error()))
+    buf = ctypes.create_string_buffer(n + 1)
+    L.ftb_device_info(device, buf, n + 1)
+    return json.loads(buf.value.decode())
+
+
 def philox_normal(ptr: int, seed: int, first: int, count: int, stream: int = 0) -> None:
     rc = lib().ftb_philox_normal(ptr, seed, first, count, stream or None)
     if rc != 0:
@@ -140,6 +153,15 @@ class EngineModel:
                         fuse_head: bool = True) -> None:
         self._check(lib().ftb_model_set_step_config(self.handle, step, tc_bn, tc_bk, tc_mh, tc_pair,
                                                     int(fuse_head)), "set_step_config")
+
+    def set_tuning(self, records) -> None:
+        """Replace the tuned kernel table: records of 9 ints
+        (step, batch_lo, batch_hi, family, tc_bn, tc_bk, tc_mh, tc_pair, fuse_head)."""
+        flat = [int(v) for r in records for v in r]
+        if any(len(r) != 9 for r in records):
+            raise ValueError("tuning records have 9 fields")
+        arr = (ctypes.c_int64 * max(1, len(flat)))(*flat)
+        self._check(lib().ftb_model_set_tuning(self.handle, ctypes.cast(arr, c_void_p), len(records)), "set_tuning")
 
     def run(self, x, out, api: int = 2) -> int:
         return int(lib().ftb_model_run(self.handle, x.ctypes.data, x.size, out.ctypes.data, out.size,

@@ -39,7 +39,7 @@ from .build_native import LIB_PATH
 from .emit import compile_shim, emit_source
 from .errors import CorrectnessError, InvalidShapeError
 from .frontend import IRGraph, export_to_ir
-from .graph_blob import POLICIES, blob_sha256, serialize
+from .graph_blob import POLICIES, blob_sha256, serialize, with_tuning
 from .runtime import NativeRuntime
 
 VALID_VARIANTS = ("naive_ijk", "loop_ikj", "tiled", "fused_ikj", "fused_tiled")
@@ -294,6 +294,31 @@ def compile_model(model: torch.nn.Module, example_inputs: Tuple[torch.Tensor, ..
         if desc["arena_bytes"] > max_workspace_bytes:
             raise ValueError("Configured max_batch_size=%d requires workspace (%d bytes arena) exceeding workspace "
                              "budget %d bytes" % (max_batch_size, desc["arena_bytes"], max_workspace_bytes))
+
+        def oracle(x: np.ndarray) -> np.ndarray:
+            with torch.no_grad():
+                y = model(torch.from_numpy(np.ascontiguousarray(x)))
+                if isinstance(y, tuple):
+                    y = y[0]
+                return y.detach().float().numpy()
+
+        ex = example_inputs[0].detach().cpu().float().numpy()
+        tuning: Dict[str, Any] = {"status": "off"}
+        if autotune:
+            if policy == "simt_exact":
+                tuning = {"status": "skipped", "reason": "gpu_kernel 'simt_exact' has one kernel per step"}
+            elif _native.device_count() == 0:
+                tuning = {"status": "skipped", "reason": "no CUDA device visible: the engine's shape rules apply"}
+            else:
+                from .autotuner import Autotuner
+                tuner = Autotuner(atol=ATOL, rtol=RTOL, device=(list(devices)[0] if devices else 0))
+                tin_shape = ((-1,) if ir.dynamic else (ex.shape[0],)) + tuple(ex.shape[1:])
+                table, treport = tuner.tune(blob, oracle, ex, tin_shape, output_dir, max_budget=max_autotune_budget,
+                                            enable_fusion=enable_fusion, tuning_batch_sizes=tuning_batch_sizes)
+                blob = with_tuning(blob, table)
+                tuning = {"status": "tuned", "cache_hit": treport.get("cache_hit", False), "table": table,
+                          "measured_speedup": treport.get("measured_speedup"),
+                          "report": os.path.join(os.path.abspath(output_dir), "autotuning_report.json")}
         gsha = blob_sha256(blob)
         cand = {"variant": variant, "gpu_kernel": policy, "enable_fusion": enable_fusion, "opt_level": opt,
                 "tile_sizes": list(tile_sizes) if tile_sizes else None}
@@ -315,7 +340,6 @@ def compile_model(model: torch.nn.Module, example_inputs: Tuple[torch.Tensor, ..
         with open(cpp_path) as f:
             source = f.read()
 
-        ex = example_inputs[0].detach().cpu().float().numpy()
         out_node = ir.nodes[ir.output_id]
         if ir.dynamic:
             in_shape = (-1,) + tuple(ex.shape[1:])
@@ -327,13 +351,6 @@ def compile_model(model: torch.nn.Module, example_inputs: Tuple[torch.Tensor, ..
         if devices:
             rt.set_devices(list(devices))
 
-        def oracle(x: np.ndarray) -> np.ndarray:
-            with torch.no_grad():
-                y = model(torch.from_numpy(np.ascontiguousarray(x)))
-                if isinstance(y, tuple):
-                    y = y[0]
-                return y.detach().float().numpy()
-
         verification: Dict[str, Any] = {"status": "skipped", "reason": "verify=False"}
         if verify:
             if _native.device_count() > 0:
@@ -343,8 +360,7 @@ def compile_model(model: torch.nn.Module, example_inputs: Tuple[torch.Tensor, ..
                 verification = {"status": "skipped", "reason": "no CUDA device visible"}
         report = {"selected_candidate": cand, "plan": {k: desc[k] for k in (
             "arena_bytes", "naive_bytes", "peak_live_bytes", "savings_percent")}, "verification": verification}
-        if autotune:
-            report["autotune"] = {"status": "heuristic", "note": "kernel family chosen per batch by the engine"}
+        report["autotune"] = tuning
         manifest = {
             "model_name": type(model).__name__,
             "input_shape": list(in_shape),

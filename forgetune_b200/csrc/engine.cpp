@@ -77,6 +77,20 @@ static constexpr char kMagicText[8] = {'F', 'T', 'B', 'G', 'R', 'A', 'P', 'H'};
 static constexpr int64_t kVersion = 1;
 static constexpr int kHeaderWords = 12;
 static constexpr int kNodeWords = 20;
+// optional trailer after the weights (8-byte aligned): magic, record count,
+// then kTuneWords int64 per record
+static constexpr char kTuneMagic[8] = {'F', 'T', 'B', 'T', 'U', 'N', 'E', '1'};
+
+std::string check_tune_record(const TuneRecord& r) {
+  if (r.batch_lo < 1 || r.batch_hi < r.batch_lo) return "batch range must satisfy 1 <= lo <= hi";
+  if (r.family < TF_HEURISTIC || r.family > TF_TCGEN05) return "family must be 0..3";
+  if (!(r.bn == 0 || r.bn == 64 || r.bn == 128 || r.bn == 256)) return "tile width must be 0, 64, 128 or 256";
+  if (!(r.bk == 0 || r.bk == 16 || r.bk == 32)) return "k-block must be 0, 16 or 32";
+  if (r.mh < 0 || r.mh > 2) return "row halves must be 0, 1 or 2";
+  if (r.pair < 0 || r.pair > 2) return "pair must be 0, 1 or 2";
+  if (r.pair == 2 && (r.mh == 2 || (r.bn != 0 && r.bn < 128))) return "SM-pair tiles need width 0, 128 or 256 and row halves 0 or 1";
+  return "";
+}
 
 Graph parse_blob(const void* data, size_t bytes) {
   if (!data || bytes < kHeaderWords * 8) throw std::runtime_error("graph blob too small");
@@ -138,6 +152,30 @@ Graph parse_blob(const void* data, size_t bytes) {
   if (g.output_id < 0 || g.output_id >= n_nodes) throw std::runtime_error("graph blob: bad output id");
   g.weights.resize(n_w);
   if (n_w) std::memcpy(g.weights.data(), base + w_off, n_w * 4);
+  const uint64_t t_off = (w_off + n_w * 4 + 7) / 8 * 8;
+  if (t_off + 16 <= bytes && std::memcmp(base + t_off, kTuneMagic, 8) == 0) {
+    int64_t n_rec = 0;
+    std::memcpy(&n_rec, base + t_off + 8, 8);
+    if (n_rec < 0 || n_rec > 1 << 16 || t_off + 16 + static_cast<uint64_t>(n_rec) * kTuneWords * 8 > bytes)
+      throw std::runtime_error("graph blob: tuning table out of range");
+    for (int64_t i = 0; i < n_rec; ++i) {
+      int64_t w[kTuneWords];
+      std::memcpy(w, base + t_off + 16 + static_cast<uint64_t>(i) * kTuneWords * 8, sizeof(w));
+      TuneRecord r;
+      r.step = w[0];
+      r.batch_lo = w[1];
+      r.batch_hi = w[2];
+      r.family = static_cast<int32_t>(w[3]);
+      r.bn = static_cast<int32_t>(w[4]);
+      r.bk = static_cast<int32_t>(w[5]);
+      r.mh = static_cast<int32_t>(w[6]);
+      r.pair = static_cast<int32_t>(w[7]);
+      r.fuse_head = w[8] != 0;
+      const std::string why = check_tune_record(r);
+      if (!why.empty()) throw std::runtime_error("graph blob: tuning record " + std::to_string(i) + ": " + why);
+      g.tuning.push_back(r);
+    }
+  }
   for (float v : g.weights)
     if (!std::isfinite(v)) throw std::runtime_error("graph blob: non-finite constant");
   return g;
@@ -551,7 +589,21 @@ Program build_program(const void* blob, size_t bytes) {
     a.head_step = static_cast<int32_t>(i + 1);
     b.head_of = static_cast<int32_t>(i);
   }
+  apply_tuning(prog.steps, g.tuning);
   return prog;
+}
+
+void apply_tuning(std::vector<Step>& steps, const std::vector<TuneRecord>& records) {
+  for (size_t i = 0; i < records.size(); ++i) {
+    const TuneRecord& r = records[i];
+    std::string why = check_tune_record(r);
+    if (why.empty() && (r.step < 0 || r.step >= static_cast<int64_t>(steps.size())))
+      why = "step index out of range";
+    if (why.empty() && steps[static_cast<size_t>(r.step)].kind != ST_GEMM) why = "step is not a GEMM";
+    if (!why.empty()) throw std::runtime_error("tuning record " + std::to_string(i) + ": " + why);
+  }
+  for (auto& st : steps) st.tuned.clear();
+  for (const auto& r : records) steps[static_cast<size_t>(r.step)].tuned.push_back(r);
 }
 
 static const char* space_name(int32_t s) {
@@ -591,7 +643,14 @@ std::string Program::describe() const {
     const auto& s = steps[i];
     os << (i ? "," : "") << "{\"kind\":" << s.kind << ",\"node\":" << s.node_id << ",\"K\":" << s.K
        << ",\"N\":" << s.N << ",\"epi\":" << s.epi << ",\"a\":\"" << space_name(s.a.space) << "\",\"out\":\""
-       << space_name(s.out.space) << "\",\"out_offset\":" << s.out.offset << "}";
+       << space_name(s.out.space) << "\",\"out_offset\":" << s.out.offset << ",\"head_step\":" << s.head_step
+       << ",\"head_of\":" << s.head_of << ",\"tuned\":[";
+    for (size_t k = 0; k < s.tuned.size(); ++k) {
+      const auto& r = s.tuned[k];
+      os << (k ? "," : "") << "[" << r.batch_lo << "," << r.batch_hi << "," << r.family << "," << r.bn << "," << r.bk
+         << "," << r.mh << "," << r.pair << "," << (r.fuse_head ? 1 : 0) << "]";
+    }
+    os << "]}";
   }
   os << "]}";
   return os.str();

@@ -93,6 +93,24 @@ enum KernelPolicy : int32_t {
   KP_TCGEN05 = 3,     // tcgen05 wherever the shape allows it
 };
 
+// One entry of a tuned kernel table: for launch-list step `step` and a
+// per-replica batch in [batch_lo, batch_hi], run this kernel family and
+// tile configuration (written by the autotuner, carried in the graph blob).
+enum TuneFamily : int32_t {
+  TF_HEURISTIC = 0,  // the engine's shape rules
+  TF_SIMT = 1,       // SIMT FFMA GEMM
+  TF_SPLITK = 2,     // split-K GEMV (batch rows <= 16)
+  TF_TCGEN05 = 3,    // tensor cores
+};
+constexpr int kTuneWords = 9;  // step, batch_lo, batch_hi, family, bn, bk, mh, pair, fuse_head
+struct TuneRecord {
+  int64_t step = 0, batch_lo = 1, batch_hi = 0;
+  int32_t family = TF_HEURISTIC, bn = 0, bk = 0, mh = 0, pair = 0;
+  bool fuse_head = true;
+};
+// Checks one record's values (not the step index); "" when valid.
+std::string check_tune_record(const TuneRecord& r);
+
 struct Graph {
   std::vector<Node> nodes;  // index == id
   int32_t input_id = -1;
@@ -102,6 +120,7 @@ struct Graph {
   int32_t kernel_policy = KP_AUTO;
   int64_t static_batch = 1;
   std::vector<float> weights;
+  std::vector<TuneRecord> tuning;  // optional trailer of the blob
 
   const Node& node(int32_t id) const { return nodes.at(static_cast<size_t>(id)); }
   Node& node(int32_t id) { return nodes.at(static_cast<size_t>(id)); }
@@ -192,6 +211,13 @@ struct Step {
   int32_t tc_mh = 0;  // 128-row halves per tile (0 = by shape)
   int32_t tc_pair = 0;  // 2 = 256-row tiles on an SM pair, 1 = one SM per tile (0 = by shape)
   bool fuse_head = true;
+  // tuned choices by batch range (GEMM steps); the first matching entry wins
+  std::vector<TuneRecord> tuned;
+  const TuneRecord* tuned_for(int64_t batch) const {
+    for (const auto& r : tuned)
+      if (batch >= r.batch_lo && batch <= r.batch_hi) return &r;
+    return nullptr;
+  }
 };
 
 constexpr int64_t kMaxHeadN = 16;
@@ -210,7 +236,11 @@ struct Program {
   std::string describe() const;  // JSON, for tests and manifests
 };
 
-// parse -> fuse -> plan -> steps
+// parse -> fuse -> plan -> steps (and the blob's tuning records onto their steps)
 Program build_program(const void* blob, size_t bytes);
+
+// Replaces the tuned tables of `steps` with `records`; throws
+// std::runtime_error naming the first invalid record.
+void apply_tuning(std::vector<Step>& steps, const std::vector<TuneRecord>& records);
 
 }  // namespace ftb

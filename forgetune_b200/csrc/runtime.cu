@@ -513,7 +513,13 @@ static int enqueue(const Model* m, const Replica* rep, ExecCtx* c, const float* 
             dispatch_simt<false, true>(a, sm, s);
         } else {
           const TcWeights& tw = rep->tc[i];
-          if (!exact && M <= 16 && c->ws_part && policy != KP_TCGEN05) {
+          // a tuned entry for this batch overrides the shape rules (never in
+          // the bit-exact policy); an entry whose family cannot run this shape
+          // falls back to them
+          const TuneRecord* tr = exact ? nullptr : st.tuned_for(batch);
+          const int fam = tr ? tr->family : TF_HEURISTIC;
+          const bool want_splitk = fam == TF_SPLITK || (fam == TF_HEURISTIC && policy != KP_TCGEN05);
+          if (!exact && M <= 16 && c->ws_part && want_splitk && fam != TF_SIMT && fam != TF_TCGEN05) {
             SplitKArgs sk{};
             sk.A = a.A;
             sk.B = a.B;
@@ -533,8 +539,9 @@ static int enqueue(const Model* m, const Replica* rep, ExecCtx* c, const float* 
             }
             if (rc == 0) break;
           }
-          const bool tc_ok = tw.maps_ready && !exact &&
-                             (policy == KP_TCGEN05 || (policy == KP_AUTO && tc_gemm_profitable(M, st.K, st.N)));
+          const bool tc_ok = tw.maps_ready && !exact && fam != TF_SIMT && fam != TF_SPLITK &&
+                             (fam == TF_TCGEN05 || policy == KP_TCGEN05 ||
+                              (policy == KP_AUTO && tc_gemm_profitable(M, st.K, st.N)));
           int tc_rc = 1;  // 1: not taken
           if (tc_ok) {
             TcArgs t{};
@@ -551,11 +558,12 @@ static int enqueue(const Model* m, const Replica* rep, ExecCtx* c, const float* 
             t.epi = st.epi;
             t.stall_test = m->tc_stall_test.load();
             TcConfig cfg;
-            cfg.bn = st.tc_bn;
-            cfg.bk = st.tc_bk;
-            cfg.mh = st.tc_mh;
-            cfg.pair = st.tc_pair;
-            if (st.head_step >= 0 && st.fuse_head) {
+            cfg.bn = tr ? tr->bn : st.tc_bn;
+            cfg.bk = tr ? tr->bk : st.tc_bk;
+            cfg.mh = tr ? tr->mh : st.tc_mh;
+            cfg.pair = tr ? tr->pair : st.tc_pair;
+            const bool fuse_head = tr ? tr->fuse_head : st.fuse_head;
+            if (st.head_step >= 0 && fuse_head) {
               const Step& hs = rep->steps[(size_t)st.head_step];
               t.head.w = ptr(hs.b);
               t.head.bias = hs.bias.space ? ptr(hs.bias) : nullptr;
@@ -1350,4 +1358,71 @@ FTB_API int ftb_small_gemm_noalloc(const float* d_x, const float* d_w, const flo
     return ST_DEVICE;
   }
   return ST_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Tuned kernel table and device description (autotuner)
+// ---------------------------------------------------------------------------
+FTB_API int ftb_model_set_tuning(void* handle, const int64_t* records, int n) {
+  auto* m = static_cast<Model*>(handle);
+  if (!m || (n > 0 && !records)) {
+    set_error("null model or records");
+    return ST_NULL;
+  }
+  if (n < 0 || n > (1 << 16)) {
+    set_error("record count out of range");
+    return ST_CONFIG;
+  }
+  std::vector<TuneRecord> recs((size_t)n);
+  for (int i = 0; i < n; ++i) {
+    const int64_t* w = records + (size_t)i * kTuneWords;
+    TuneRecord& r = recs[(size_t)i];
+    r.step = w[0];
+    r.batch_lo = w[1];
+    r.batch_hi = w[2];
+    r.family = (int32_t)w[3];
+    r.bn = (int32_t)w[4];
+    r.bk = (int32_t)w[5];
+    r.mh = (int32_t)w[6];
+    r.pair = (int32_t)w[7];
+    r.fuse_head = w[8] != 0;
+  }
+  std::lock_guard<std::mutex> lk(m->mu);
+  try {
+    apply_tuning(m->prog.steps, recs);
+    for (auto& rep : m->replicas) apply_tuning(rep->steps, recs);
+  } catch (const std::exception& e) {
+    set_error(e.what());
+    return ST_CONFIG;
+  }
+  for (ExecCtx* c : m->all_ctxs) {
+    for (auto& cg : c->graphs) cudaGraphExecDestroy(cg.exec);
+    c->graphs.clear();
+  }
+  return ST_OK;
+}
+
+FTB_API int ftb_device_info(int device, char* buf, size_t cap) {
+  cudaDeviceProp prop;
+  if (cudaGetDeviceProperties(&prop, device) != cudaSuccess) {
+    set_error(std::string("no CUDA device ") + std::to_string(device));
+    return ST_DEVICE;
+  }
+  int drv = 0, rt = 0;
+  cudaDriverGetVersion(&drv);
+  cudaRuntimeGetVersion(&rt);
+  std::string name(prop.name);
+  for (char& ch : name)
+    if (ch == '"' || ch == '\\') ch = ' ';
+  const std::string js = "{\"name\":\"" + name + "\",\"cc\":\"" + std::to_string(prop.major) + "." +
+                         std::to_string(prop.minor) + "\",\"sm_count\":" + std::to_string(prop.multiProcessorCount) +
+                         ",\"memory_bytes\":" + std::to_string((unsigned long long)prop.totalGlobalMem) +
+                         ",\"driver_version\":" + std::to_string(drv) + ",\"runtime_version\":" + std::to_string(rt) +
+                         "}";
+  if (buf && cap > 0) {
+    const size_t k = std::min(cap - 1, js.size());
+    std::memcpy(buf, js.data(), k);
+    buf[k] = 0;
+  }
+  return (int)js.size();
 }

@@ -51,6 +51,39 @@ def _live_nodes(g: IRGraph) -> List[int]:
     return sorted(keep)
 
 
+TUNE_MAGIC = b"FTBTUNE1"
+TUNE_WORDS = 9  # step, batch_lo, batch_hi, family, tc_bn, tc_bk, tc_mh, tc_pair, fuse_head
+
+
+def with_tuning(blob: bytes, records) -> bytes:
+    """The blob with its tuning trailer replaced by ``records`` (none: removed).
+
+    The trailer follows the weights at the next 8-byte boundary: the magic
+    ``FTBTUNE1``, the record count and 9 little-endian int64 per record."""
+    _, version, n_nodes = struct.unpack_from("<8sqq", blob, 0)
+    n_w, _, w_off = struct.unpack_from("<3q", blob, 9 * 8)
+    end = (w_off + n_w * 4 + 7) // 8 * 8
+    out = bytearray(blob[:w_off + n_w * 4])
+    out += b"\0" * (end - len(out))
+    if records:
+        out += TUNE_MAGIC + struct.pack("<q", len(records))
+        for r in records:
+            if len(r) != TUNE_WORDS:
+                raise ValueError("tuning records have %d fields" % TUNE_WORDS)
+            out += struct.pack("<%dq" % TUNE_WORDS, *[int(v) for v in r])
+    return bytes(out)
+
+
+def tuning_of(blob: bytes):
+    """The tuning records carried by a blob (empty list when it has none)."""
+    n_w, _, w_off = struct.unpack_from("<3q", blob, 9 * 8)
+    end = (w_off + n_w * 4 + 7) // 8 * 8
+    if len(blob) < end + 16 or blob[end:end + 8] != TUNE_MAGIC:
+        return []
+    (n,) = struct.unpack_from("<q", blob, end + 8)
+    return [list(struct.unpack_from("<%dq" % TUNE_WORDS, blob, end + 16 + i * TUNE_WORDS * 8)) for i in range(n)]
+
+
 def serialize(g: IRGraph, *, enable_fusion: bool, bias_first_fused: bool, kernel_policy: str = "auto",
               fold_epilogues: bool = True) -> bytes:
     live = _live_nodes(g)

@@ -130,6 +130,19 @@ FORGETUNE_EXPORT int ftb_model_set_policy(void* model, int policy);
  * gives bit-identical results. */
 FORGETUNE_EXPORT int ftb_model_set_step_config(void* model, int step, int tc_bn, int tc_bk, int tc_mh, int tc_pair,
                                                int fuse_head);
+/* Tuned kernel table (the autotuner's result): n records of 9 int64 each,
+ *   {step, batch_lo, batch_hi, family, tc_bn, tc_bk, tc_mh, tc_pair, fuse_head}
+ * For GEMM launch-list step `step` and a per-device batch in
+ * [batch_lo, batch_hi] the first matching record picks the kernel family
+ * (0 = the engine's shape rules, 1 = SIMT FFMA, 2 = split-K GEMV for at most
+ * 16 rows, 3 = tensor cores) and the tensor-core tile as in
+ * ftb_model_set_step_config; a family that cannot run the shape falls back to
+ * the shape rules.  Replaces the whole table (n = 0 clears it); ignored by
+ * the bit-exact policy.  The same records can be carried in the graph blob
+ * (a trailer after the weights), which is how a compiled model keeps its
+ * tuning.  No counterpart in the reference (its autotuner picks among
+ * generated C++ variants at compile time: python/forgetune/autotuner.py). */
+FORGETUNE_EXPORT int ftb_model_set_tuning(void* model, const int64_t* records, int n);
 FORGETUNE_EXPORT int ftb_model_prepare(void* model);
 /* Failure-detection hook (tests): while tc_stall != 0 every tensor-core
  * launch of the model makes one pipeline wait that nothing completes run out
@@ -158,6 +171,10 @@ FORGETUNE_EXPORT void ftb_model_reset_counters(void* model);
 FORGETUNE_EXPORT void ftb_model_inject_alloc(void* model);
 FORGETUNE_EXPORT int ftb_model_describe(void* model, char* buf, size_t cap);
 FORGETUNE_EXPORT int ftb_device_count(void);
+/* JSON description of CUDA device `device` (name, compute capability, SM
+ * count, memory, driver and runtime versions) into buf; returns its length or
+ * a negative status.  The autotuner's cache key uses it. */
+FORGETUNE_EXPORT int ftb_device_info(int device, char* buf, size_t cap);
 /* Elements [first, first+count) of the Philox4x32-10 N(0,1) stream keyed by
  * seed, written to device memory on `stream` (the wide-MLP input generator). */
 FORGETUNE_EXPORT int ftb_philox_normal(float* d_out, uint64_t seed, uint64_t first, uint64_t count, void* stream);
