@@ -451,12 +451,15 @@ inline int launch_tc_gemm(const TcArgs& t, const TcWeights& w, int* err, int sm_
   if (!w.maps_ready || t.M <= 0) return 1;
   if (t.M > 0x7fffffff / 2 || t.N > 65535 * 64) return 1;
   const int bn = cfg.bn ? cfg.bn : tc_choose_bn(t.M, t.N, sm_count, t.head.n > 0);
-  const int bk = cfg.bk ? cfg.bk : 16;
-  // 256-row tiles on SM pairs when there are enough of them to occupy every
-  // pair (they move a third less operand data per MMA through shared memory);
-  // one SM per tile otherwise
+  // 256-row tiles on SM pairs for tiles of 128 or 256 columns: they move a
+  // third less operand data per MMA through shared memory, and when there
+  // are fewer tiles than pairs the last round's column slices spread them
+  // over more SMs than one-SM tiles would use
   const int64_t pair_tiles = ((t.M + 255) / 256) * ((t.N + bn - 1) / bn);
-  const bool pair = cfg.pair == 2 || (cfg.pair == 0 && cfg.mh != 2 && pair_tiles >= sm_count / 2);
+  const bool pair = cfg.pair == 2 || (cfg.pair == 0 && cfg.mh != 2 && bn >= 128);
+  // k-blocks of 32 when the tiles do not fill the pairs (fewer, larger stages
+  // per tile), 16 (deeper ring) otherwise
+  const int bk = cfg.bk ? cfg.bk : (pair && pair_tiles < sm_count / 2 ? 32 : 16);
   if (pair && bn >= 128) {
     if (bk == 32) return bn == 128 ? launch_tc_pair_bn<128, 32, 4>(t, w, err, s) : launch_tc_pair_bn<256, 32, 3>(t, w, err, s);
     return bn == 128 ? launch_tc_pair_bn<128, 16, 8>(t, w, err, s) : launch_tc_pair_bn<256, 16, 6>(t, w, err, s);
