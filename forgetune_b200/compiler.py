@@ -225,21 +225,115 @@ def _verify(rt: NativeRuntime, oracle, example: np.ndarray, dynamic: bool, max_b
     return report
 
 
-def compile_model(model: torch.nn.Module, example_inputs: Tuple[torch.Tensor, ...],
-                  output_dir: str = "build/artifacts/model", autotune: bool = True, max_autotune_budget: int = 8,
-                  compiler_opt_level: str = "-O2", kernel_variant: Optional[str] = None,
-                  enable_fusion: bool = False, tile_sizes: Optional[Tuple[int, int, int]] = None,
-                  dynamic_batch: bool = False, max_batch_size: int = 128,
-                  max_workspace_bytes: int = 512 * 1024 * 1024, tuning_batch_sizes: Optional[List[int]] = None,
-                  gpu_kernel: Optional[str] = None, devices: Optional[Sequence[int]] = None,
-                  verify: bool = True) -> CompiledModel:
-    """Compile ``model`` into a GPU-backed shared library with the reference C ABI.
+def _module_oracle(model: torch.nn.Module):
+    def oracle(x: np.ndarray) -> np.ndarray:
+        with torch.no_grad():
+            y = model(torch.from_numpy(np.ascontiguousarray(x)))
+            if isinstance(y, tuple):
+                y = y[0]
+            return y.detach().float().numpy()
+    return oracle
 
-    Arguments and checks follow the reference's ``compile_model``.  Additions:
-    ``gpu_kernel`` ('auto', 'simt', 'simt_exact', 'tcgen05'; default 'auto'),
-    ``devices`` (CUDA device ids to shard the batch over) and ``verify``
-    (run the differential gate when a CUDA device is present).
-    """
+
+def _compile_ir(ir: IRGraph, oracle, ex: np.ndarray, output_dir: str, model_name: str, autotune: bool,
+                max_autotune_budget: int, opt: str, variant: str, enable_fusion: bool,
+                tile_sizes: Optional[Tuple[int, int, int]], max_workspace_bytes: int,
+                tuning_batch_sizes: Optional[List[int]], policy: str, devices: Optional[Sequence[int]],
+                verify: bool) -> CompiledModel:
+    """IR -> graph blob (autotuned on the GPU when asked) -> per-model library
+    -> runtime, with the correctness gate against ``oracle``."""
+    os.makedirs(output_dir, exist_ok=True)
+    max_batch_size = ir.max_batch_size
+    bias_first = variant in ("fused_ikj", "loop_ikj")
+    blob = serialize(ir, enable_fusion=enable_fusion, bias_first_fused=bias_first, kernel_policy=policy)
+    desc = _native.describe_blob(blob)
+    if desc["arena_bytes"] > max_workspace_bytes:
+        raise ValueError("Configured max_batch_size=%d requires workspace (%d bytes arena) exceeding workspace "
+                         "budget %d bytes" % (max_batch_size, desc["arena_bytes"], max_workspace_bytes))
+
+    tuning: Dict[str, Any] = {"status": "off"}
+    if autotune:
+        if policy == "simt_exact":
+            tuning = {"status": "skipped", "reason": "gpu_kernel 'simt_exact' has one kernel per step"}
+        elif _native.device_count() == 0:
+            tuning = {"status": "skipped", "reason": "no CUDA device visible: the engine's shape rules apply"}
+        else:
+            from .autotuner import Autotuner
+            tuner = Autotuner(atol=ATOL, rtol=RTOL, device=(list(devices)[0] if devices else 0))
+            tin_shape = ((-1,) if ir.dynamic else (ex.shape[0],)) + tuple(ex.shape[1:])
+            table, treport = tuner.tune(blob, oracle, ex, tin_shape, output_dir, max_budget=max_autotune_budget,
+                                        enable_fusion=enable_fusion, tuning_batch_sizes=tuning_batch_sizes)
+            blob = with_tuning(blob, table)
+            tuning = {"status": "tuned", "cache_hit": treport.get("cache_hit", False), "table": table,
+                      "measured_speedup": treport.get("measured_speedup"),
+                      "report": os.path.join(os.path.abspath(output_dir), "autotuning_report.json")}
+    gsha = blob_sha256(blob)
+    cand = {"variant": variant, "gpu_kernel": policy, "enable_fusion": enable_fusion, "opt_level": opt,
+            "tile_sizes": list(tile_sizes) if tile_sizes else None}
+    prov = hashlib.sha256(json.dumps({"graph": gsha, "cand": cand, "engine": engine_fingerprint()},
+                                     sort_keys=True).encode()).hexdigest()[:12]
+    cand_dir = os.path.abspath(os.path.join(output_dir, "%s_%s" % (variant, prov)))
+    os.makedirs(cand_dir, exist_ok=True)
+    blob_path = os.path.join(cand_dir, "graph.ftb")
+    cpp_path = os.path.join(cand_dir, "model.cpp")
+    so_path = os.path.join(cand_dir, "kernel_%s.so" % prov)
+    if not os.path.isfile(so_path):
+        with open(blob_path + ".tmp", "wb") as f:
+            f.write(blob)
+        os.replace(blob_path + ".tmp", blob_path)
+        src = emit_source(blob_path, len(blob), gsha, ir.dynamic, desc["max_batch"])
+        with open(cpp_path, "w") as f:
+            f.write(src)
+        compile_shim(cpp_path, so_path, opt)
+    with open(cpp_path) as f:
+        source = f.read()
+
+    out_node = ir.nodes[ir.output_id]
+    if ir.dynamic:
+        in_shape = (-1,) + tuple(ex.shape[1:])
+        out_shape = tuple(-1 if (i == 0 and out_node.shape[0] == -1) else s for i, s in enumerate(out_node.shape))
+    else:
+        in_shape = tuple(ex.shape)
+        out_shape = tuple(out_node.shape)
+    rt = NativeRuntime(so_path, in_shape, out_shape)
+    if devices:
+        rt.set_devices(list(devices))
+
+    verification: Dict[str, Any] = {"status": "skipped", "reason": "verify=False"}
+    if verify:
+        if _native.device_count() > 0:
+            verification = _verify(rt, oracle, ex, ir.dynamic, desc["max_batch"])
+            verification["status"] = "passed"
+        else:
+            verification = {"status": "skipped", "reason": "no CUDA device visible"}
+    report = {"selected_candidate": cand, "plan": {k: desc[k] for k in (
+        "arena_bytes", "naive_bytes", "peak_live_bytes", "savings_percent")}, "verification": verification}
+    report["autotune"] = tuning
+    manifest = {
+        "model_name": model_name,
+        "input_shape": list(in_shape),
+        "output_shape": list(out_shape),
+        "kernel_config": cand,
+        "artifacts": {"shared_library": so_path, "graph_blob": blob_path, "source": cpp_path,
+                      "so_sha256": _sha_file(so_path), "graph_sha256": gsha},
+        "graph_hash": gsha,
+        "provenance_hash": prov,
+        "engine_fingerprint": engine_fingerprint(),
+        "platform": sys.platform,
+        "machine": platform.machine(),
+        "optimization_summary": report,
+    }
+    tmp = os.path.join(output_dir, "manifest.json.tmp")
+    with open(tmp, "w") as f:
+        json.dump(manifest, f, indent=2)
+    os.replace(tmp, os.path.join(output_dir, "manifest.json"))
+    return CompiledModel(rt, manifest, source, report)
+
+
+def _check_options(autotune, max_autotune_budget, compiler_opt_level, kernel_variant, enable_fusion, tile_sizes,
+                   dynamic_batch, max_batch_size, max_workspace_bytes, gpu_kernel) -> Tuple[str, str, str]:
+    """The reference compile_model's argument checks (compiler.py:440-520);
+    returns (opt level, kernel variant, gpu kernel policy)."""
     if type(max_autotune_budget) is not int or not 1 <= max_autotune_budget <= 8:
         raise ValueError("max_autotune_budget must be an integer between 1 and 8, got %r" % (max_autotune_budget,))
     if type(max_batch_size) is not int or not 1 <= max_batch_size <= 1_000_000:
@@ -276,6 +370,27 @@ def compile_model(model: torch.nn.Module, example_inputs: Tuple[torch.Tensor, ..
     policy = gpu_kernel or "auto"
     if policy not in GPU_KERNELS:
         raise ValueError("Unknown gpu_kernel '%s'. Valid: %s" % (policy, list(GPU_KERNELS)))
+    return opt, variant, policy
+
+
+def compile_model(model: torch.nn.Module, example_inputs: Tuple[torch.Tensor, ...],
+                  output_dir: str = "build/artifacts/model", autotune: bool = True, max_autotune_budget: int = 8,
+                  compiler_opt_level: str = "-O2", kernel_variant: Optional[str] = None,
+                  enable_fusion: bool = False, tile_sizes: Optional[Tuple[int, int, int]] = None,
+                  dynamic_batch: bool = False, max_batch_size: int = 128,
+                  max_workspace_bytes: int = 512 * 1024 * 1024, tuning_batch_sizes: Optional[List[int]] = None,
+                  gpu_kernel: Optional[str] = None, devices: Optional[Sequence[int]] = None,
+                  verify: bool = True) -> CompiledModel:
+    """Compile ``model`` into a GPU-backed shared library with the reference C ABI.
+
+    Arguments and checks follow the reference's ``compile_model``.  Additions:
+    ``gpu_kernel`` ('auto', 'simt', 'simt_exact', 'tcgen05'; default 'auto'),
+    ``devices`` (CUDA device ids to shard the batch over) and ``verify``
+    (run the differential gate when a CUDA device is present).
+    """
+    opt, variant, policy = _check_options(autotune, max_autotune_budget, compiler_opt_level, kernel_variant,
+                                          enable_fusion, tile_sizes, dynamic_batch, max_batch_size,
+                                          max_workspace_bytes, gpu_kernel)
     for name, p in model.named_parameters():
         if p.device.type != "cpu":
             raise ValueError("Model parameter '%s' is on device '%s'; compile from CPU parameters." % (name, p.device))
@@ -283,104 +398,46 @@ def compile_model(model: torch.nn.Module, example_inputs: Tuple[torch.Tensor, ..
         if not isinstance(t, torch.Tensor) or t.device.type != "cpu":
             raise ValueError("Example input %d must be a CPU tensor." % i)
 
-    os.makedirs(output_dir, exist_ok=True)
     modes = {n: m.training for n, m in model.named_modules()}
     try:
         model.eval()
         ir: IRGraph = export_to_ir(model, example_inputs, dynamic_batch=dynamic_batch, max_batch_size=max_batch_size)
-        bias_first = variant in ("fused_ikj", "loop_ikj")
-        blob = serialize(ir, enable_fusion=enable_fusion, bias_first_fused=bias_first, kernel_policy=policy)
-        desc = _native.describe_blob(blob)
-        if desc["arena_bytes"] > max_workspace_bytes:
-            raise ValueError("Configured max_batch_size=%d requires workspace (%d bytes arena) exceeding workspace "
-                             "budget %d bytes" % (max_batch_size, desc["arena_bytes"], max_workspace_bytes))
-
-        def oracle(x: np.ndarray) -> np.ndarray:
-            with torch.no_grad():
-                y = model(torch.from_numpy(np.ascontiguousarray(x)))
-                if isinstance(y, tuple):
-                    y = y[0]
-                return y.detach().float().numpy()
-
+        oracle = _module_oracle(model)
         ex = example_inputs[0].detach().cpu().float().numpy()
-        tuning: Dict[str, Any] = {"status": "off"}
-        if autotune:
-            if policy == "simt_exact":
-                tuning = {"status": "skipped", "reason": "gpu_kernel 'simt_exact' has one kernel per step"}
-            elif _native.device_count() == 0:
-                tuning = {"status": "skipped", "reason": "no CUDA device visible: the engine's shape rules apply"}
-            else:
-                from .autotuner import Autotuner
-                tuner = Autotuner(atol=ATOL, rtol=RTOL, device=(list(devices)[0] if devices else 0))
-                tin_shape = ((-1,) if ir.dynamic else (ex.shape[0],)) + tuple(ex.shape[1:])
-                table, treport = tuner.tune(blob, oracle, ex, tin_shape, output_dir, max_budget=max_autotune_budget,
-                                            enable_fusion=enable_fusion, tuning_batch_sizes=tuning_batch_sizes)
-                blob = with_tuning(blob, table)
-                tuning = {"status": "tuned", "cache_hit": treport.get("cache_hit", False), "table": table,
-                          "measured_speedup": treport.get("measured_speedup"),
-                          "report": os.path.join(os.path.abspath(output_dir), "autotuning_report.json")}
-        gsha = blob_sha256(blob)
-        cand = {"variant": variant, "gpu_kernel": policy, "enable_fusion": enable_fusion, "opt_level": opt,
-                "tile_sizes": list(tile_sizes) if tile_sizes else None}
-        prov = hashlib.sha256(json.dumps({"graph": gsha, "cand": cand, "engine": engine_fingerprint()},
-                                         sort_keys=True).encode()).hexdigest()[:12]
-        cand_dir = os.path.abspath(os.path.join(output_dir, "%s_%s" % (variant, prov)))
-        os.makedirs(cand_dir, exist_ok=True)
-        blob_path = os.path.join(cand_dir, "graph.ftb")
-        cpp_path = os.path.join(cand_dir, "model.cpp")
-        so_path = os.path.join(cand_dir, "kernel_%s.so" % prov)
-        if not os.path.isfile(so_path):
-            with open(blob_path + ".tmp", "wb") as f:
-                f.write(blob)
-            os.replace(blob_path + ".tmp", blob_path)
-            src = emit_source(blob_path, len(blob), gsha, ir.dynamic, desc["max_batch"])
-            with open(cpp_path, "w") as f:
-                f.write(src)
-            compile_shim(cpp_path, so_path, opt)
-        with open(cpp_path) as f:
-            source = f.read()
-
-        out_node = ir.nodes[ir.output_id]
-        if ir.dynamic:
-            in_shape = (-1,) + tuple(ex.shape[1:])
-            out_shape = tuple(-1 if (i == 0 and out_node.shape[0] == -1) else s for i, s in enumerate(out_node.shape))
-        else:
-            in_shape = tuple(ex.shape)
-            out_shape = tuple(out_node.shape)
-        rt = NativeRuntime(so_path, in_shape, out_shape)
-        if devices:
-            rt.set_devices(list(devices))
-
-        verification: Dict[str, Any] = {"status": "skipped", "reason": "verify=False"}
-        if verify:
-            if _native.device_count() > 0:
-                verification = _verify(rt, oracle, ex, ir.dynamic, desc["max_batch"])
-                verification["status"] = "passed"
-            else:
-                verification = {"status": "skipped", "reason": "no CUDA device visible"}
-        report = {"selected_candidate": cand, "plan": {k: desc[k] for k in (
-            "arena_bytes", "naive_bytes", "peak_live_bytes", "savings_percent")}, "verification": verification}
-        report["autotune"] = tuning
-        manifest = {
-            "model_name": type(model).__name__,
-            "input_shape": list(in_shape),
-            "output_shape": list(out_shape),
-            "kernel_config": cand,
-            "artifacts": {"shared_library": so_path, "graph_blob": blob_path, "source": cpp_path,
-                          "so_sha256": _sha_file(so_path), "graph_sha256": gsha},
-            "graph_hash": gsha,
-            "provenance_hash": prov,
-            "engine_fingerprint": engine_fingerprint(),
-            "platform": sys.platform,
-            "machine": platform.machine(),
-            "optimization_summary": report,
-        }
-        tmp = os.path.join(output_dir, "manifest.json.tmp")
-        with open(tmp, "w") as f:
-            json.dump(manifest, f, indent=2)
-        os.replace(tmp, os.path.join(output_dir, "manifest.json"))
-        return CompiledModel(rt, manifest, source, report)
+        return _compile_ir(ir, oracle, ex, output_dir, type(model).__name__, autotune, max_autotune_budget, opt,
+                           variant, enable_fusion, tile_sizes, max_workspace_bytes, tuning_batch_sizes, policy,
+                           devices, verify)
     finally:
         for n, m in model.named_modules():
             if n in modes:
                 m.training = modes[n]
+
+
+def compile_graph_json(graph_json, output_dir: str = "build/artifacts/graph", example_input: Optional[np.ndarray] = None,
+                       autotune: bool = True, max_autotune_budget: int = 8, compiler_opt_level: str = "-O2",
+                       kernel_variant: Optional[str] = None, enable_fusion: bool = False,
+                       tile_sizes: Optional[Tuple[int, int, int]] = None,
+                       max_workspace_bytes: int = 512 * 1024 * 1024, tuning_batch_sizes: Optional[List[int]] = None,
+                       gpu_kernel: Optional[str] = None, devices: Optional[Sequence[int]] = None,
+                       verify: bool = True) -> CompiledModel:
+    """Compile a reference ``graph.json`` (schema 2.0: a path, the text or the
+    parsed dict, as the reference frontend or CLI writes it) like
+    ``compile_model``.  The batch mode and max_batch_size come from the graph;
+    the correctness gate and the autotuner compare with a float64 NumPy
+    evaluation of the graph (``ir_json.evaluate``).  ``example_input``
+    defaults to two rows (or the static batch) of seeded normal values."""
+    from .ir_json import evaluate, load_graph_json
+    ir = load_graph_json(graph_json)
+    opt, variant, policy = _check_options(autotune, max_autotune_budget, compiler_opt_level, kernel_variant,
+                                          enable_fusion, tile_sizes, ir.dynamic, ir.max_batch_size,
+                                          max_workspace_bytes, gpu_kernel)
+    in_shape = ir.nodes[ir.input_id].shape
+    if example_input is None:
+        rows = min(2, ir.max_batch_size) if ir.dynamic else in_shape[0]
+        example_input = np.random.default_rng(1).standard_normal((rows,) + tuple(in_shape[1:])).astype(np.float32)
+    ex = np.ascontiguousarray(example_input, dtype=np.float32)
+    if tuple(ex.shape[1:]) != tuple(in_shape[1:]) or (not ir.dynamic and ex.shape[0] != in_shape[0]):
+        raise InvalidShapeError("example input shape %s does not match the graph input %s" % (ex.shape, in_shape))
+    return _compile_ir(ir, lambda x: evaluate(ir, x), ex, output_dir, "graph_json", autotune, max_autotune_budget,
+                       opt, variant, enable_fusion, tile_sizes, max_workspace_bytes, tuning_batch_sizes, policy,
+                       devices, verify)
