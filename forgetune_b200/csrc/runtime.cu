@@ -31,6 +31,7 @@
 #include "simt_gemm.cuh"
 #include "splitk_gemv.cuh"
 #include "tc_pair_gemm.cuh"
+#include "conv_tc.cuh"
 
 #define FTB_API extern "C" __attribute__((visibility("default")))
 
@@ -107,6 +108,10 @@ struct ExecCtx {
   // split-K workspace inside the block: partial sums and per-column-block tickets
   float* ws_part = nullptr;
   unsigned* ws_tickets = nullptr;
+  // tensor-core convolution: im2col rows and GEMM output for conv_imgs images
+  float* ws_col = nullptr;
+  float* ws_cout = nullptr;
+  int64_t conv_imgs = 0;
   bool in_use = false;
   struct CachedGraph {
     int64_t batch;
@@ -200,6 +205,18 @@ static thread_local ThreadPools t_pools;
 
 static ThreadPool& pool_of(Model* m, int dev) { return t_pools.pools[PoolKey{m->uid, dev}]; }
 
+// A convolution the tensor-core path can run: its im2col GEMM has N = Cout
+// >= 32 output columns, and its epilogue is per output channel (a residual
+// or [M, N] bias would be indexed in NCHW, which the GEMM rows are not).
+static bool conv_tc_candidate(const Step& s) {
+  return s.kind == ST_CONV && s.N >= 32 && !(s.epi & (EPI_RESIDUAL | EPI_BIAS_ROWS)) &&
+         tc_gemm_supported(tc_padded_k(s.K), s.N);
+}
+
+// Workspace budget of the tensor-core convolution per context: the images of
+// one chunk, im2col rows plus GEMM output.
+static constexpr size_t kConvWorkspaceBytes = 256u << 20;
+
 // ---------------------------------------------------------------------------
 // replica creation: upload weights and derived layouts
 // ---------------------------------------------------------------------------
@@ -259,6 +276,22 @@ static int make_replica(Model* m, int dev, Replica** out) {
       for (int64_t co = 0; co < s.N; ++co)
         for (int64_t k = 0; k < s.K; ++k) host[off + k * s.N + co] = w[co * s.K + k];
       s.w_kn = off;
+      if (m->allow_tc && conv_tc_candidate(s)) {
+        // OIHW is already W^T [Cout, K]: tf32 hi / lo rows padded to Kp
+        const int64_t Kp = tc_padded_k(s.K);
+        s.Kp = Kp;
+        const size_t hi = append((size_t)s.N * Kp, 64);
+        const size_t lo = append((size_t)s.N * Kp, 64);
+        for (int64_t co = 0; co < s.N; ++co)
+          for (int64_t k = 0; k < s.K; ++k) {
+            const float v = w[co * s.K + k];
+            const float h = tf32_round_host(v);
+            host[hi + co * Kp + k] = h;
+            host[lo + co * Kp + k] = tf32_round_host(v - h);
+          }
+        s.w_nk_hi = hi;
+        s.w_nk_lo = lo;
+      }
       // k -> (input offset, dh*kh, dw*kw)
       ktab_off[i] = append((size_t)s.K * 4, 16);
       int32_t* t = reinterpret_cast<int32_t*>(host.data() + ktab_off[i]);
@@ -287,7 +320,7 @@ static int make_replica(Model* m, int dev, Replica** out) {
       c.ktab = reinterpret_cast<const int4*>(rep->weights + ktab_off[i]);
       rep->conv[i] = c;
     }
-    if (s.kind == ST_GEMM && s.w_nk_hi) {
+    if ((s.kind == ST_GEMM || s.kind == ST_CONV) && s.w_nk_hi) {
       rep->tc[i].hi = rep->weights + s.w_nk_hi;
       rep->tc[i].lo = rep->weights + s.w_nk_lo;
       rep->tc[i].Kp = s.Kp;
@@ -339,7 +372,24 @@ static int layout_block(Model* m, ExecCtx* c, size_t min_bytes, bool* did_alloc)
     if (st.kind == ST_GEMM) max_n = std::max(max_n, st.N);
   const size_t part_b = round256((size_t)kSkMaxSlices * 16 * (size_t)max_n * sizeof(float));
   const size_t tick_b = round256((size_t)((max_n + kSkCols - 1) / kSkCols + 1) * sizeof(unsigned));
-  const size_t need = std::max(arena + in_b + out_b + part_b + tick_b, min_bytes);
+  // tensor-core convolution: one chunk of images, sized for the largest step
+  size_t img_col = 0, img_out = 0;
+  int64_t conv_max_imgs = 0;
+  if (m->allow_tc)
+    for (const Step& st : p.steps)
+      if (conv_tc_candidate(st)) {
+        img_col = std::max(img_col, (size_t)(st.Ho * st.Wo) * (size_t)tc_padded_k(st.K) * sizeof(float));
+        img_out = std::max(img_out, (size_t)(st.Ho * st.Wo) * (size_t)st.N * sizeof(float));
+        conv_max_imgs = std::max<int64_t>(conv_max_imgs, st.static_rows ? st.rows_per_sample : p.max_batch);
+      }
+  int64_t conv_imgs = 0;
+  if (img_col) {
+    conv_imgs = (int64_t)std::max<size_t>(1, kConvWorkspaceBytes / (img_col + img_out));
+    conv_imgs = std::min<int64_t>(std::min<int64_t>(conv_imgs, conv_max_imgs), 65535);
+  }
+  const size_t col_b = round256((size_t)conv_imgs * img_col);
+  const size_t cout_b = round256((size_t)conv_imgs * img_out);
+  const size_t need = std::max(arena + in_b + out_b + part_b + tick_b + col_b + cout_b, min_bytes);
   bool fresh = false;
   if (!c->block || c->block_bytes < need) {
     int rc = alloc_block(c, need);
@@ -354,6 +404,10 @@ static int layout_block(Model* m, ExecCtx* c, size_t min_bytes, bool* did_alloc)
   c->d_out = reinterpret_cast<float*>(c->block + arena + in_b);
   c->ws_part = max_n ? reinterpret_cast<float*>(c->block + arena + in_b + out_b) : nullptr;
   c->ws_tickets = max_n ? reinterpret_cast<unsigned*>(c->block + arena + in_b + out_b + part_b) : nullptr;
+  c->conv_imgs = conv_imgs;
+  c->ws_col = conv_imgs ? reinterpret_cast<float*>(c->block + arena + in_b + out_b + part_b + tick_b) : nullptr;
+  c->ws_cout = conv_imgs ? reinterpret_cast<float*>(c->block + arena + in_b + out_b + part_b + tick_b + col_b)
+                         : nullptr;
   if (fresh && c->ws_tickets) {
     // tickets start at zero; every split-K launch leaves them at zero
     if (cudaMemset(c->ws_tickets, 0, tick_b) != cudaSuccess) {
@@ -469,6 +523,44 @@ static void copy_floats(const float* a, float* y, int64_t n, int sm, cudaStream_
 // Enqueues the launch list for `batch` rows on stream s.  With `marks`
 // (steps + 1 events) an event is recorded before every step and after the
 // last one, so per-step device times can be read back afterwards.
+// Convolution step on the tensor cores, in chunks of c->conv_imgs images:
+// im2col rows -> 3xTF32 GEMM (bias / ReLU epilogue per output channel) ->
+// NCHW.  Returns 0 when launched, 1 when the GEMM declines the shape (the
+// caller runs the SIMT convolution), -1 on a launch error.
+static int run_tc_conv(const Model* m, const Replica* rep, ExecCtx* c, const Step& st, const GemmArgs& a,
+                       const TcWeights& tw, int64_t imgs, int sm, cudaStream_t s) {
+  const int HoWo = (int)(st.Ho * st.Wo);
+  const int Kp = (int)st.Kp;
+  const int64_t in_img = st.Cin * st.H * st.W, out_img = st.N * (int64_t)HoWo;
+  for (int64_t b0 = 0; b0 < imgs; b0 += c->conv_imgs) {
+    const int64_t nb = std::min<int64_t>(c->conv_imgs, imgs - b0);
+    if (launch_im2col(a.A + b0 * in_img, c->ws_col, a.conv, (int)st.K, Kp, nb * HoWo, sm, s)) return -1;
+    TcArgs t{};
+    t.A = c->ws_col;
+    t.w_hi = tw.hi;
+    t.w_lo = tw.lo;
+    t.bias = a.bias;
+    t.res = nullptr;
+    t.Y = c->ws_cout;
+    t.M = nb * HoWo;
+    t.N = st.N;
+    t.K = Kp;
+    t.Kp = Kp;
+    t.epi = st.epi;
+    t.stall_test = m->tc_stall_test.load();
+    TcConfig cfg;
+    cfg.bn = st.tc_bn;
+    cfg.bk = st.tc_bk;
+    cfg.mh = st.tc_mh;
+    cfg.pair = st.tc_pair;
+    const int rc = launch_tc_gemm(t, tw, rep->err_dev, sm, s, cfg);
+    if (rc == 1 && b0 == 0) return 1;
+    if (rc != 0) return -1;
+    if (launch_rows_to_nchw(c->ws_cout, a.Y + b0 * out_img, nb, HoWo, (int)st.N, s)) return -1;
+  }
+  return 0;
+}
+
 static int enqueue(const Model* m, const Replica* rep, ExecCtx* c, const float* in, float* out, int64_t batch,
                    cudaStream_t s, cudaEvent_t* marks = nullptr) {
   char* arena = c->arena;
@@ -507,10 +599,26 @@ static int enqueue(const Model* m, const Replica* rep, ExecCtx* c, const float* 
         a.M = (int)M;
         if (st.kind == ST_CONV) {
           a.conv = rep->conv[i];
-          if (exact)
+          const TcWeights& tw = rep->tc[i];
+          int tc_rc = 1;  // 1: not taken
+          // convolutions of 32 output channels too: their im2col GEMMs have
+          // many rows, and the SIMT convolution is what they replace
+          if (!exact && tw.maps_ready && c->ws_col &&
+              (policy == KP_TCGEN05 || (policy == KP_AUTO && M >= 128 && st.N >= 32 && st.Kp >= 32))) {
+            tc_rc = run_tc_conv(m, rep, c, st, a, tw, st.static_rows ? st.rows_per_sample : batch, sm, s);
+            if (tc_rc < 0) {
+              set_error(std::string("tensor-core convolution launch failed: ") +
+                        cudaGetErrorString(cudaGetLastError()));
+              return ST_DEVICE;
+            }
+          }
+          if (tc_rc == 0) {
+            // im2col + tensor-core GEMM + NCHW
+          } else if (exact) {
             dispatch_simt<true, true>(a, sm, s);
-          else
+          } else {
             dispatch_simt<false, true>(a, sm, s);
+          }
         } else {
           const TcWeights& tw = rep->tc[i];
           // a tuned entry for this batch overrides the shape rules (never in

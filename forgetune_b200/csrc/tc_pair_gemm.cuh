@@ -458,8 +458,9 @@ inline int launch_tc_gemm(const TcArgs& t, const TcWeights& w, int* err, int sm_
   const int64_t pair_tiles = ((t.M + 255) / 256) * ((t.N + bn - 1) / bn);
   const bool pair = cfg.pair == 2 || (cfg.pair == 0 && cfg.mh != 2 && bn >= 128);
   // k-blocks of 32 when the tiles do not fill the pairs (fewer, larger stages
-  // per tile), 16 (deeper ring) otherwise
-  const int bk = cfg.bk ? cfg.bk : (pair && pair_tiles < sm_count / 2 ? 32 : 16);
+  // per tile) or K is long (measured on 4096/8192-deep layers: the per-k-block
+  // overheads matter more than ring depth), 16 (deeper ring) otherwise
+  const int bk = cfg.bk ? cfg.bk : (pair && (pair_tiles < sm_count / 2 || t.K >= 4096) ? 32 : 16);
   if (pair && bn >= 128) {
     if (bk == 32) return bn == 128 ? launch_tc_pair_bn<128, 32, 4>(t, w, err, s) : launch_tc_pair_bn<256, 32, 3>(t, w, err, s);
     return bn == 128 ? launch_tc_pair_bn<128, 16, 8>(t, w, err, s) : launch_tc_pair_bn<256, 16, 6>(t, w, err, s);

@@ -147,3 +147,37 @@ def test_fused_head_on_sm_pairs_agrees(M, K, H, N2, tmp_path):
     assert np.array_equal(outs[0].view(np.uint32), outs[1].view(np.uint32))
     eng.close()
     cm.close()
+
+
+CONVS = [
+    # B, Cin, H, W, Cout, k, stride, pad, dilation, relu
+    (256, 3, 32, 32, 32, 3, 1, 1, 1, True),      # the CNN's first layer: K = 27 padded to 32
+    (256, 32, 32, 32, 64, 3, 2, 1, 1, True),     # second: stride 2
+    (64, 64, 8, 8, 64, 3, 2, 1, 1, False),
+    (7, 5, 13, 11, 40, 3, 1, 2, 2, True),        # dilation 2, Cout not a multiple of 32, odd sizes
+    (3, 8, 9, 9, 48, 1, 1, 0, 1, False),         # 1x1
+    (100, 16, 64, 64, 32, 3, 1, 1, 1, True),     # workspace chunks: ~80 images per chunk
+]
+
+
+@pytest.mark.parametrize("B,Cin,H,W,Cout,k,stride,pad,dil,relu", CONVS)
+def test_tcgen05_convolution_matches_oracle(B, Cin, H, W, Cout, k, stride, pad, dil, relu, tmp_path):
+    """Convolution as im2col rows + the 3xTF32 GEMM + NCHW, against the oracle's
+    direct convolution with the reference's tolerance, bitwise run to run."""
+    torch.manual_seed(Cin * 100 + Cout)
+    layers = [nn.Conv2d(Cin, Cout, k, stride=stride, padding=pad, dilation=dil)]
+    if relu:
+        layers.append(nn.ReLU())
+    m = nn.Sequential(*layers).eval()
+    cm = compile_model(m, (torch.randn(2, Cin, H, W),), output_dir=str(tmp_path), autotune=False,
+                       enable_fusion=True, kernel_variant="fused_ikj", dynamic_batch=True, max_batch_size=B,
+                       max_workspace_bytes=8 << 30, gpu_kernel="tcgen05", verify=False)
+    x = np.random.default_rng(B + Cout).standard_normal((B, Cin, H, W)).astype(np.float32)
+    got = cm.run(x)
+    conv = m[0]
+    want = oracle.conv2d(x, conv.weight.detach().numpy(), conv.bias.detach().numpy(), (stride, stride), (pad, pad),
+                         (dil, dil), relu=relu)
+    assert got.shape == want.shape
+    assert np.allclose(got, want, atol=1e-4, rtol=1e-4), float(np.max(np.abs(got - want)))
+    assert np.array_equal(got.view(np.uint32), cm.run(x).view(np.uint32))
+    cm.close()
