@@ -112,6 +112,9 @@ struct ExecCtx {
   float* ws_col = nullptr;
   float* ws_cout = nullptr;
   int64_t conv_imgs = 0;
+  // split-K partial sums of the SM-pair tensor-core GEMM
+  float* ws_ksplit = nullptr;
+  size_t ws_ksplit_floats = 0;
   bool in_use = false;
   struct CachedGraph {
     int64_t batch;
@@ -216,6 +219,9 @@ static bool conv_tc_candidate(const Step& s) {
 // Workspace budget of the tensor-core convolution per context: the images of
 // one chunk, im2col rows plus GEMM output.
 static constexpr size_t kConvWorkspaceBytes = 256u << 20;
+// Split-K partial sums per context (see launch_tc_pair_bn): 74 pairs x 256
+// rows x 256 columns of fp32 covers every split it chooses on a B200.
+static constexpr size_t kKsplitWorkspaceFloats = (size_t)74 * 256 * 256;
 
 // ---------------------------------------------------------------------------
 // replica creation: upload weights and derived layouts
@@ -389,7 +395,15 @@ static int layout_block(Model* m, ExecCtx* c, size_t min_bytes, bool* did_alloc)
   }
   const size_t col_b = round256((size_t)conv_imgs * img_col);
   const size_t cout_b = round256((size_t)conv_imgs * img_out);
-  const size_t need = std::max(arena + in_b + out_b + part_b + tick_b + col_b + cout_b, min_bytes);
+  // split-K partial sums: it runs only when at most half the SM pairs have a
+  // whole 256-row tile, so at most 74 x 256 x 256 floats
+  bool any_tc = false;
+  if (m->allow_tc)
+    for (const Step& st : p.steps)
+      if ((st.kind == ST_GEMM && tc_gemm_supported(st.K, st.N)) || conv_tc_candidate(st)) any_tc = true;
+  const size_t ks_floats = any_tc ? kKsplitWorkspaceFloats : 0;
+  const size_t ks_b = round256(ks_floats * sizeof(float));
+  const size_t need = std::max(arena + in_b + out_b + part_b + tick_b + col_b + cout_b + ks_b, min_bytes);
   bool fresh = false;
   if (!c->block || c->block_bytes < need) {
     int rc = alloc_block(c, need);
@@ -408,6 +422,10 @@ static int layout_block(Model* m, ExecCtx* c, size_t min_bytes, bool* did_alloc)
   c->ws_col = conv_imgs ? reinterpret_cast<float*>(c->block + arena + in_b + out_b + part_b + tick_b) : nullptr;
   c->ws_cout = conv_imgs ? reinterpret_cast<float*>(c->block + arena + in_b + out_b + part_b + tick_b + col_b)
                          : nullptr;
+  c->ws_ksplit_floats = ks_floats;
+  c->ws_ksplit = ks_floats ? reinterpret_cast<float*>(c->block + arena + in_b + out_b + part_b + tick_b + col_b +
+                                                      cout_b)
+                           : nullptr;
   if (fresh && c->ws_tickets) {
     // tickets start at zero; every split-K launch leaves them at zero
     if (cudaMemset(c->ws_tickets, 0, tick_b) != cudaSuccess) {
@@ -548,6 +566,8 @@ static int run_tc_conv(const Model* m, const Replica* rep, ExecCtx* c, const Ste
     t.Kp = Kp;
     t.epi = st.epi;
     t.stall_test = m->tc_stall_test.load();
+    t.ws = c->ws_ksplit;
+    t.ws_floats = c->ws_ksplit_floats;
     TcConfig cfg;
     cfg.bn = st.tc_bn;
     cfg.bk = st.tc_bk;
@@ -665,6 +685,8 @@ static int enqueue(const Model* m, const Replica* rep, ExecCtx* c, const float* 
             t.Kp = tw.Kp;
             t.epi = st.epi;
             t.stall_test = m->tc_stall_test.load();
+            t.ws = c->ws_ksplit;
+            t.ws_floats = c->ws_ksplit_floats;
             TcConfig cfg;
             cfg.bn = tr ? tr->bn : st.tc_bn;
             cfg.bk = tr ? tr->bk : st.tc_bk;
@@ -1048,11 +1070,11 @@ FTB_API int ftb_model_set_step_config(void* handle, int step, int tc_bn, int tc_
     return ST_CONFIG;
   }
   if (!(tc_bn == 0 || tc_bn == 64 || tc_bn == 128 || tc_bn == 256) || !(tc_bk == 0 || tc_bk == 16 || tc_bk == 32) ||
-      !(tc_mh >= 0 && tc_mh <= 2) || !(tc_pair >= 0 && tc_pair <= 2)) {
-    set_error("tile width must be 0, 64, 128 or 256, k-block 0, 16 or 32, row halves 0, 1 or 2, pair 0, 1 or 2");
+      !(tc_mh >= 0 && tc_mh <= 2) || !(tc_pair >= 0 && tc_pair <= 3)) {
+    set_error("tile width must be 0, 64, 128 or 256, k-block 0, 16 or 32, row halves 0, 1 or 2, pair 0..3");
     return ST_CONFIG;
   }
-  if (tc_pair == 2 && (tc_mh == 2 || (tc_bn != 0 && tc_bn < 128))) {
+  if (tc_pair >= 2 && (tc_mh == 2 || (tc_bn != 0 && tc_bn < 128))) {
     set_error("SM-pair tiles are 256 rows by 128 or 256 columns (row halves 0 or 1)");
     return ST_CONFIG;
   }

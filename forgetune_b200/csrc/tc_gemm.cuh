@@ -64,6 +64,8 @@ struct TcHead {
 };
 
 struct TcArgs {
+  float* ws = nullptr;     // split-K partial sums (SM-pair kernel), ws_floats capacity
+  size_t ws_floats = 0;
   const float* A;
   const float* w_hi;
   const float* w_lo;
@@ -88,6 +90,11 @@ struct TcKernelParams {
   // SM-pair kernel: tiles from split_from on run as `split` column slices
   int split;
   int split_from;
+  // SM-pair kernel, split-K: every tile runs as `ksplit` units of `kb_per`
+  // k-blocks each; unit s writes its raw sums to slice s of the output map
+  // (a [ksplit, M, N] workspace) and a reduction finishes them
+  int ksplit;
+  int kb_per;
   // test hook: the MMA thread first waits on a barrier nothing completes, so
   // the bounded wait runs out and the abort path runs (failure-detection tests)
   int stall_test;
@@ -374,10 +381,11 @@ __device__ __forceinline__ void epi_group(float (&e)[4], uint32_t epi, const flo
   }
 }
 
-__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int c0, int c1) {
-  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+// TMA store of a staged box to (column c0, row c1, slice c2) of the output map
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void* src, int c0, int c1, int c2) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%1, %2, %3}], [%4];" ::"l"(
                    reinterpret_cast<uint64_t>(map)),
-               "r"(c0), "r"(c1), "r"(smem_u32(src))
+               "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(src))
                : "memory");
 }
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
@@ -458,10 +466,12 @@ __device__ __forceinline__ void tc_head_rows(const TcKernelParams& p, const TcEp
 // warp's 128-byte-swizzled staging tile and one lane stores the 32 x 32 block
 // with TMA (which clips at the matrix edges); else the block is transposed
 // through shared memory so each store instruction writes 128 contiguous bytes.
+// `epi` replaces p.epi (0 for split-K partial sums, which the reduction
+// finishes); `slice` is the split-K slice the TMA store writes.
 template <int BN>
 __device__ __forceinline__ void tc_epilogue_block(const TcKernelParams& p, const CUtensorMap* map_y,
                                                   const TcEpiSmem& e, uint32_t base, int m0, int n0, int width,
-                                                  int q, int lane) {
+                                                  int q, int lane, uint32_t epi_all, int slice) {
   if (e.hn > 0) {
     const int m = m0 + q * 32 + lane;
     switch (e.hp) {
@@ -486,7 +496,7 @@ __device__ __forceinline__ void tc_epilogue_block(const TcKernelParams& p, const
       const int cnt = min(32, p.N - n);
       const int64_t off = (int64_t)(row_ok ? m : 0) * p.N + n;
       // rows past M load nothing of the [M, N] operands; TMA drops them
-      const uint32_t epi = row_ok ? p.epi : (p.epi & ~(uint32_t)(EPI_BIAS_ROWS | EPI_RESIDUAL));
+      const uint32_t epi = row_ok ? epi_all : (epi_all & ~(uint32_t)(EPI_BIAS_ROWS | EPI_RESIDUAL));
       const float* bsrc = (epi & EPI_BIAS_ROWS) ? p.bias + off : p.bias + n;
       const bool bvec = cnt == 32 && aligned16(bsrc);
       const bool rvec = cnt == 32 && aligned16(p.res + off);
@@ -504,7 +514,7 @@ __device__ __forceinline__ void tc_epilogue_block(const TcKernelParams& p, const
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) {
-        tma_store_2d(map_y, stage, n, m0 + q * 32);
+        tma_store_3d(map_y, stage, n, m0 + q * 32, slice);
         bulk_commit();
       }
     }
@@ -526,7 +536,7 @@ __device__ __forceinline__ void tc_epilogue_block(const TcKernelParams& p, const
       const int rows = min(32, p.M - (m0 + q * 32));
       for (int i = 0; i < rows; ++i) {
         const int m = m0 + q * 32 + i;
-        p.Y[(int64_t)m * p.N + n] = apply_epilogue(tr[i * 33 + lane], p.epi, p.bias, p.res, m, n, p.N);
+        p.Y[(int64_t)m * p.N + n] = apply_epilogue(tr[i * 33 + lane], epi_all, p.bias, p.res, m, n, p.N);
       }
     }
   }
@@ -716,7 +726,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
       for (int h = 0; h < MH; ++h) {
         const int m0 = (t / tiles_n) * BMT + h * kTcBM;
         tc_epilogue_block<BN>(p, &map_y, e, tmem + (buf * MH + h) * (uint32_t)BN + ((uint32_t)(q * 32) << 16), m0,
-                              n0, BN, q, lane);
+                              n0, BN, q, lane, p.epi, 0);
       }
       tc_fence_before();
       __syncwarp();
@@ -730,6 +740,34 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
     __syncwarp();
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+  }
+}
+
+// Split-K reduction: y[m, n] = epi(sum over s = 0 .. S-1, in order, of
+// part[s, m, n]); four columns per thread.
+__global__ void __launch_bounds__(256) tc_splitk_reduce_kernel(const float* __restrict__ part, int S, int M, int N,
+                                                               uint32_t epi, const float* __restrict__ bias,
+                                                               const float* __restrict__ res, float* __restrict__ Y) {
+  const int64_t quads = (int64_t)M * (N / 4);
+  const int64_t plane = (int64_t)M * N;
+  for (int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; q < quads; q += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t m = q / (N / 4);
+    const int n = (int)(q - m * (N / 4)) * 4;
+    const int64_t off = m * N + n;
+    float4 acc = *reinterpret_cast<const float4*>(part + off);
+    for (int s = 1; s < S; ++s) {
+      const float4 v = *reinterpret_cast<const float4*>(part + s * plane + off);
+      acc.x = __fadd_rn(acc.x, v.x);
+      acc.y = __fadd_rn(acc.y, v.y);
+      acc.z = __fadd_rn(acc.z, v.z);
+      acc.w = __fadd_rn(acc.w, v.w);
+    }
+    float4 out;
+    out.x = apply_epilogue(acc.x, epi, bias, res, m, n + 0, N);
+    out.y = apply_epilogue(acc.y, epi, bias, res, m, n + 1, N);
+    out.z = apply_epilogue(acc.z, epi, bias, res, m, n + 2, N);
+    out.w = apply_epilogue(acc.w, epi, bias, res, m, n + 3, N);
+    *reinterpret_cast<float4*>(Y + off) = out;
   }
 }
 
@@ -767,6 +805,23 @@ inline bool make_map_2d(CUtensorMap* map, const float* base, int64_t rows, int64
              CU_TENSOR_MAP_INTERLEAVE_NONE, bk == 32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
+
+// Output map: [slices, rows, cols] fp32 row-major, box 32 x 32 x 1, 128-byte
+// swizzle (the epilogue's staging tile layout).  Rows are clipped per slice.
+inline bool make_map_3d_out(CUtensorMap* map, float* base, int64_t slices, int64_t rows, int64_t cols) {
+  PFN_encodeTiled enc = tma_encoder();
+  if (!enc) return false;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || (cols * 4) % 16) return false;
+  cuuint64_t dims[3] = {(cuuint64_t)cols, (cuuint64_t)rows, (cuuint64_t)slices};
+  cuuint64_t strides[2] = {(cuuint64_t)(cols * 4), (cuuint64_t)(rows * cols * 4)};
+  cuuint32_t box[3] = {32, 32, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+inline int tc_bk_index(int bk) { return bk == 32 ? 0 : 1; }
 
 inline int tc_bn_index(int bn) { return bn == 64 ? 0 : bn == 128 ? 1 : 2; }
 
@@ -816,7 +871,9 @@ inline int launch_tc_bn(const TcArgs& t, const TcWeights& w, int* err, int sm_co
   // then only the head's small outputs are written)
   CUtensorMap map_y;
   std::memset(&map_y, 0, sizeof(map_y));
-  p.y_tma = (t.head.n == 0 && make_map_2d(&map_y, t.Y, t.M, t.N, t.N, 32, 32)) ? 1 : 0;
+  p.y_tma = (t.head.n == 0 && make_map_3d_out(&map_y, t.Y, 1, t.M, t.N)) ? 1 : 0;
+  p.ksplit = 1;
+  p.kb_per = 0;
   // the accumulator starts at zero: a bias-first epilogue adds the bias at the end
   if (p.epi & EPI_BIAS_FIRST) p.epi = (p.epi & ~(uint32_t)EPI_BIAS_FIRST) | EPI_BIAS_LAST;
   if (p.head.epi & EPI_BIAS_FIRST) p.head.epi = (p.head.epi & ~(uint32_t)EPI_BIAS_FIRST) | EPI_BIAS_LAST;

@@ -129,15 +129,30 @@ __device__ __forceinline__ uint32_t idesc_tf32_pair(int n) {
 // `npairs`; when the last round is partial, its tiles are cut into `split`
 // column slices of BN / split so that more pairs share it (a slice is the
 // same MMAs on fewer columns: the results do not change).
+// With split-K (ksplit > 1, no column slices) every tile is instead cut
+// into ksplit units of kb_per k-blocks, unit s of a tile covering k-blocks
+// [s kb_per, (s+1) kb_per) and writing slice s of the partial sums.
 struct PairWork {
   int tiles_n;  // tiles per row block
   int full;     // units [0, full) are whole tiles, tile = unit
   int split;    // the tiles from `full` on are cut into this many slices
+  int ksplit;   // k ranges per tile (1: none)
+  int kb_per;   // k-blocks per range
+  int nk;       // k-blocks of the whole K
   int units;
-  __device__ __forceinline__ void unit(int u, int bn, int& m0, int& n0, int& width) const {
+  __device__ __forceinline__ void unit(int u, int bn, int& m0, int& n0, int& width, int& kb0, int& kb1,
+                                       int& slice) const {
     int tile = u, part = 0;
     width = bn;
-    if (u >= full) {
+    slice = 0;
+    kb0 = 0;
+    kb1 = nk;
+    if (ksplit > 1) {
+      tile = u / ksplit;
+      slice = u % ksplit;
+      kb0 = slice * kb_per;
+      kb1 = min(nk, kb0 + kb_per);
+    } else if (u >= full) {
       tile = full + (u - full) / split;
       part = (u - full) % split;
       width = bn / split;
@@ -197,12 +212,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
   const int tiles_m = (p.M + 255) / 256;
   const int tiles_n = (p.N + BN - 1) / BN;
   const int ntiles = tiles_m * tiles_n;
+  const int nk = (p.K + BK - 1) / BK;
   PairWork work;
   work.tiles_n = tiles_n;
-  work.split = p.split > 1 ? p.split : 1;
+  work.nk = nk;
+  work.ksplit = p.ksplit > 1 ? p.ksplit : 1;
+  work.kb_per = work.ksplit > 1 ? p.kb_per : nk;
+  work.split = (p.split > 1 && work.ksplit == 1) ? p.split : 1;
   work.full = work.split > 1 ? p.split_from : ntiles;
-  work.units = work.full + (ntiles - work.full) * work.split;
-  const int nk = (p.K + BK - 1) / BK;
+  work.units = work.ksplit > 1 ? ntiles * work.ksplit : work.full + (ntiles - work.full) * work.split;
   const int pair = (int)cluster_index();
   const int npairs = (int)cluster_count();
 
@@ -239,13 +257,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
     uint32_t it = 0;
     bool ok = true;
     for (int u = pair; u < work.units && ok; u += npairs) {
-      int m0, n0, width;
-      work.unit(u, BN, m0, n0, width);
+      int m0, n0, width, kb0, kb1, slice;
+      work.unit(u, BN, m0, n0, width, kb0, kb1, slice);
       m0 += (int)rank * kTcBM;
       // this CTA's half of the unit's W^T rows (a narrower slice loads the
       // full BN/2-row box; the MMA reads only its first width/2 rows)
       const int nb = n0 + (int)rank * (width / 2);
-      for (int kb = 0; kb < nk; ++kb, ++it) {
+      for (int kb = kb0; kb < kb1; ++kb, ++it) {
         const int s = (int)(it % STAGES);
         const uint32_t r = it / STAGES;
         if (!(ok = pair_wait_warp(&empty[s], (r & 1u) ^ 1u, abort_flag, peer_abort, p.err, 1))) break;
@@ -264,14 +282,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
       bool ok = true;
       if (p.stall_test) ok = pair_wait_warp(never, 0, abort_flag, peer_abort, p.err, 9);
       for (int u = pair; u < work.units && ok; u += npairs, ++tc) {
-        int m0, n0, width;
-        work.unit(u, BN, m0, n0, width);
+        int m0, n0, width, kb0, kb1, slice;
+        work.unit(u, BN, m0, n0, width, kb0, kb1, slice);
         const uint32_t idesc = idesc_tf32_pair(width);
         const uint32_t buf = tc & 1u, use = tc >> 1;
         if (!(ok = pair_wait_warp(&acce[buf], (use & 1u) ^ 1u, abort_flag, peer_abort, p.err, 2))) break;
         tc_fence_after();
         const uint32_t d = tmem + buf * (uint32_t)BN;
-        for (int kb = 0; kb < nk; ++kb, ++it) {
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = (int)(it % STAGES);
           const uint32_t par = (it / STAGES) & 1u;
           if (!(ok = pair_wait_warp(&conv[s], par, abort_flag, peer_abort, p.err, 4))) break;
@@ -285,7 +303,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
               const uint32_t off = (uint32_t)j * 32u;
               const uint64_t dbh = smem_desc_sw<BK>(bhi + off), dbl = smem_desc_sw<BK>(blo + off);
               const uint64_t dah = smem_desc_sw<BK>(ahi + off), dal = smem_desc_sw<BK>(alo + off);
-              umma2_tf32(d, dah, dbh, idesc, (kb > 0 || j > 0) ? 1u : 0u);
+              umma2_tf32(d, dah, dbh, idesc, (kb > kb0 || j > 0) ? 1u : 0u);
               umma2_tf32(d, dah, dbl, idesc, 1u);
               umma2_tf32(d, dal, dbh, idesc, 1u);
             }
@@ -318,7 +336,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
     uint32_t it = 0;
     bool ok = true;
     for (int u = pair; u < work.units && ok; u += npairs) {
-      for (int kb = 0; kb < nk; ++kb, ++it) {
+      int m0, n0, width, kb0, kb1, slice;
+      work.unit(u, BN, m0, n0, width, kb0, kb1, slice);
+      for (int kb = kb0; kb < kb1; ++kb, ++it) {
         const int s = (int)(it % STAGES);
         if (!(ok = pair_wait_warp(&full[s], (it / STAGES) & 1u, abort_flag, peer_abort, p.err, 6))) break;
         tc_split_a<(kTcBM * BK / 4) / 128>(reinterpret_cast<float4*>(a_tile(s)),
@@ -337,11 +357,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
       const uint32_t buf = tc & 1u, use = tc >> 1;
       if (!pair_wait_warp(&accf[buf], use & 1u, abort_flag, peer_abort, p.err, 7)) break;
       tc_fence_after();
-      int m0, n0, width;
-      work.unit(u, BN, m0, n0, width);
+      int m0, n0, width, kb0, kb1, slice;
+      work.unit(u, BN, m0, n0, width, kb0, kb1, slice);
       m0 += (int)rank * kTcBM;
+      // split-K units store raw sums into their slice; the reduction applies the epilogue
       tc_epilogue_block<BN>(p, &map_y, e, tmem + buf * (uint32_t)BN + ((uint32_t)(q * 32) << 16), m0, n0, width, q,
-                            lane);
+                            lane, work.ksplit > 1 ? 0u : p.epi, slice);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(cluster_addr(&acce[buf], 0));
@@ -386,7 +407,7 @@ inline int tc_pair_prepare(int* max_pairs) {
 // Returns 0 when launched, 1 when this GEMM cannot take this path, -1 on a
 // launch error.
 template <int BN, int BK, int STAGES>
-inline int launch_tc_pair_bn(const TcArgs& t, const TcWeights& w, int* err, cudaStream_t s) {
+inline int launch_tc_pair_bn(const TcArgs& t, const TcWeights& w, int* err, cudaStream_t s, bool ksplit_ok) {
   using L = TcPairSmem<BN, BK, STAGES>;
   int max_pairs = 0;
   if (tc_pair_prepare<BN, BK, STAGES>(&max_pairs) != 0) return -1;
@@ -407,11 +428,50 @@ inline int launch_tc_pair_bn(const TcArgs& t, const TcWeights& w, int* err, cuda
   // then only the head's small outputs are written)
   CUtensorMap map_y;
   std::memset(&map_y, 0, sizeof(map_y));
-  p.y_tma = (t.head.n == 0 && make_map_2d(&map_y, t.Y, t.M, t.N, t.N, 32, 32)) ? 1 : 0;
+  p.y_tma = (t.head.n == 0 && make_map_3d_out(&map_y, t.Y, 1, t.M, t.N)) ? 1 : 0;
+  p.ksplit = 1;
+  p.kb_per = 0;
   if (p.epi & EPI_BIAS_FIRST) p.epi = (p.epi & ~(uint32_t)EPI_BIAS_FIRST) | EPI_BIAS_LAST;
   if (p.head.epi & EPI_BIAS_FIRST) p.head.epi = (p.head.epi & ~(uint32_t)EPI_BIAS_FIRST) | EPI_BIAS_LAST;
   if (p.head.n > 0 && (t.N > BN || p.head.n > kTcMaxHeadN || t.N > kTcMaxHeadK)) return 1;
   const int64_t ntiles = ((t.M + 255) / 256) * ((t.N + BN - 1) / BN);
+  // split-K when asked (ksplit_ok), the whole tiles cannot occupy half the
+  // pairs and K is long (32 k-blocks or more: on shorter K the reduction pass
+  // and the shorter pipelines cost more than the extra pairs give, measured
+  // on 784- and 512-deep layers): S k-ranges per tile of at least 8 k-blocks
+  // each, at most 16, their partial sums fitting the workspace, reduced in
+  // slice order
+  const int nk = (int)((t.K + BK - 1) / BK);
+  const bool y_ok = (t.N * 4) % 16 == 0 && (reinterpret_cast<uintptr_t>(t.Y) & 15) == 0;
+  const bool wants_ksplit = ksplit_ok && y_ok && t.ws && ntiles * 2 <= max_pairs && nk >= 32;
+  // a fused head needs whole rows: when the shape wants split-K, decline the
+  // fused form (the caller then runs the GEMM with split-K and the head as its
+  // own step, much cheaper than one tile walking the whole K)
+  if (wants_ksplit && t.head.n > 0) return 1;
+  if (wants_ksplit && p.y_tma) {
+    int S = (int)std::min<int64_t>(std::min<int64_t>(max_pairs / ntiles, nk / 8), 16);
+    while (S > 1 && (size_t)S * (size_t)t.M * (size_t)t.N > t.ws_floats) --S;
+    if (S > 1) {
+      const int kb_per = (nk + S - 1) / S;
+      S = (nk + kb_per - 1) / kb_per;  // no empty ranges
+      CUtensorMap map_ws;
+      if (S > 1 && make_map_3d_out(&map_ws, t.ws, S, t.M, t.N)) {
+        p.ksplit = S;
+        p.kb_per = kb_per;
+        p.split = 1;
+        p.split_from = (int)ntiles;
+        const unsigned pairs = (unsigned)std::min<int64_t>(ntiles * S, max_pairs);
+        tc_pair_gemm_kernel<BN, BK, STAGES><<<2 * pairs, kTcThreads, L::TOTAL, s>>>(
+            map_a, w.map_hi[tc_bk_index(BK)][tc_bn_index(BN / 2)], w.map_lo[tc_bk_index(BK)][tc_bn_index(BN / 2)],
+            map_ws, p);
+        if (cudaGetLastError() != cudaSuccess) return -1;
+        const int64_t quads = t.M * (t.N / 4);
+        const int grid = (int)std::min<int64_t>(std::max<int64_t>((quads + 255) / 256, 1), (int64_t)max_pairs * 16);
+        tc_splitk_reduce_kernel<<<grid, 256, 0, s>>>(t.ws, S, (int)t.M, (int)t.N, p.epi, p.bias, p.res, p.Y);
+        return cudaGetLastError() == cudaSuccess ? 0 : -1;
+      }
+    }
+  }
   // the last, partial round of tiles: cut into the slice count (1, 2 or 4,
   // slices at least 32 columns wide) that ends it soonest; not with a fused
   // head, which needs whole rows
@@ -443,7 +503,8 @@ struct TcConfig {
   int bn = 0;    // 64, 128 or 256
   int bk = 0;    // 16 or 32
   int mh = 0;    // one-SM tile rows: 1 -> 128, 2 -> 256 (two M=128 MMAs share each W k-block)
-  int pair = 0;  // 1 = one SM per tile, 2 = 256-row tiles on an SM pair (BN 128 or 256)
+  int pair = 0;  // 1 = one SM per tile, 2 = 256-row tiles on an SM pair (BN 128 or 256),
+                 // 3 = SM pair, split-K when the tiles cannot occupy the pairs
 };
 
 inline int launch_tc_gemm(const TcArgs& t, const TcWeights& w, int* err, int sm_count, cudaStream_t s,
@@ -456,14 +517,20 @@ inline int launch_tc_gemm(const TcArgs& t, const TcWeights& w, int* err, int sm_
   // are fewer tiles than pairs the last round's column slices spread them
   // over more SMs than one-SM tiles would use
   const int64_t pair_tiles = ((t.M + 255) / 256) * ((t.N + bn - 1) / bn);
-  const bool pair = cfg.pair == 2 || (cfg.pair == 0 && cfg.mh != 2 && bn >= 128);
+  const bool pair = cfg.pair >= 2 || (cfg.pair == 0 && cfg.mh != 2 && bn >= 128);
+  // split-K (a different summation order) only where the caller allows it:
+  // the shape rules (0) and the explicit SM-pair-with-split-K choice (3)
+  const bool ksplit_ok = cfg.pair == 0 || cfg.pair == 3;
   // k-blocks of 32 when the tiles do not fill the pairs (fewer, larger stages
   // per tile) or K is long (measured on 4096/8192-deep layers: the per-k-block
   // overheads matter more than ring depth), 16 (deeper ring) otherwise
   const int bk = cfg.bk ? cfg.bk : (pair && (pair_tiles < sm_count / 2 || t.K >= 4096) ? 32 : 16);
   if (pair && bn >= 128) {
-    if (bk == 32) return bn == 128 ? launch_tc_pair_bn<128, 32, 4>(t, w, err, s) : launch_tc_pair_bn<256, 32, 3>(t, w, err, s);
-    return bn == 128 ? launch_tc_pair_bn<128, 16, 8>(t, w, err, s) : launch_tc_pair_bn<256, 16, 6>(t, w, err, s);
+    if (bk == 32)
+      return bn == 128 ? launch_tc_pair_bn<128, 32, 4>(t, w, err, s, ksplit_ok)
+                       : launch_tc_pair_bn<256, 32, 3>(t, w, err, s, ksplit_ok);
+    return bn == 128 ? launch_tc_pair_bn<128, 16, 8>(t, w, err, s, ksplit_ok)
+                     : launch_tc_pair_bn<256, 16, 6>(t, w, err, s, ksplit_ok);
   }
   const int mh = (cfg.mh == 2 && bn <= 128) ? 2 : 1;
   if (mh == 2) {

@@ -123,11 +123,14 @@ FORGETUNE_EXPORT int ftb_model_set_devices(void* model, const int* device_ids, i
 FORGETUNE_EXPORT int ftb_model_set_policy(void* model, int policy);
 /* Tensor-core tile of launch-list step `step`: width tc_bn (0, 64, 128, 256),
  * k-block tc_bk (0, 16, 32), rows tc_mh x 128 on one SM (0, 1, 2; 2 needs
- * tc_bn <= 128), tc_pair (0, 1, 2): 2 = 256-row tiles computed by an SM pair
- * (tcgen05 cta_group::2; needs tc_bn 0, 128 or 256 and tc_mh 0 or 1), 1 = one
- * SM per tile; 0 = chosen by shape.  fuse_head: compute a following small-N
- * head in the epilogue.  For the autotuner; call between runs.  Every choice
- * gives bit-identical results. */
+ * tc_bn <= 128), tc_pair (0..3): 2 = 256-row tiles computed by an SM pair
+ * (tcgen05 cta_group::2; needs tc_bn 0, 128 or 256 and tc_mh 0 or 1), 3 = the
+ * same with split-K when the tiles cannot occupy the pairs (k ranges summed
+ * in a fixed order), 1 = one SM per tile; 0 = chosen by shape (may pick
+ * split-K).  fuse_head: compute a following small-N head in the epilogue.
+ * For the autotuner; call between runs.  The choices other than split-K give
+ * bit-identical results; split-K changes the order of the k sums (still
+ * deterministic run to run). */
 FORGETUNE_EXPORT int ftb_model_set_step_config(void* model, int step, int tc_bn, int tc_bk, int tc_mh, int tc_pair,
                                                int fuse_head);
 /* Tuned kernel table (the autotuner's result): n records of 9 int64 each,

@@ -181,3 +181,37 @@ def test_tcgen05_convolution_matches_oracle(B, Cin, H, W, Cout, k, stride, pad, 
     assert np.allclose(got, want, atol=1e-4, rtol=1e-4), float(np.max(np.abs(got - want)))
     assert np.array_equal(got.view(np.uint32), cm.run(x).view(np.uint32))
     cm.close()
+
+
+@pytest.mark.parametrize("M,K,N,relu,residual", [(256, 4096, 128, True, False), (1024, 512, 512, False, True),
+                                                 (300, 2048, 256, True, False), (17, 1024, 132, False, False)])
+@pytest.mark.parametrize("pair", [0, 3])
+def test_split_k_matches_oracle(M, K, N, relu, residual, pair, tmp_path):
+    """Few tiles and a long K: the SM-pair kernel splits K into ranges whose
+    partial sums a reduction adds in a fixed order (shape rules, pair=0, and
+    the explicit choice, pair=3); within tolerance of the oracle, bitwise run
+    to run."""
+    from forgetune_b200 import _native
+    torch.manual_seed(M + K)
+    m = Block(K, N, relu, residual).eval() if not residual else Block(K, K, relu, True).eval()
+    n_out = K if residual else N
+    cm = compile_model(m, (torch.randn(2, K),), output_dir=str(tmp_path), autotune=False, enable_fusion=True,
+                       kernel_variant="fused_ikj", dynamic_batch=True, max_batch_size=max(M, 2),
+                       gpu_kernel="tcgen05", verify=False)
+    with open(cm.manifest()["artifacts"]["graph_blob"], "rb") as f:
+        eng = _native.EngineModel(f.read())
+    eng.set_devices([torch.cuda.current_device()])
+    eng.set_step_config(0, 0, 0, 0, pair, True)
+    x = np.random.default_rng(K).standard_normal((M, K)).astype(np.float32)
+    y = np.zeros((M, n_out), np.float32)
+    assert eng.run(x, y) == 0, _native.last_error()
+    want = oracle.gemm(x, m.fc.weight.detach().numpy().T.copy(), m.fc.bias.detach().numpy(), relu=relu,
+                       order="bias_last")
+    if residual:
+        want = oracle.add(want, x)
+    assert np.allclose(y, want, atol=1e-4, rtol=1e-4), float(np.max(np.abs(y - want)))
+    y2 = np.zeros_like(y)
+    assert eng.run(x, y2) == 0
+    assert np.array_equal(y.view(np.uint32), y2.view(np.uint32))
+    eng.close()
+    cm.close()
