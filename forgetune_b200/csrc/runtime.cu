@@ -32,6 +32,7 @@
 #include "splitk_gemv.cuh"
 #include "tc_pair_gemm.cuh"
 #include "conv_tc.cuh"
+#include "narrow_gemm.cuh"
 
 #define FTB_API extern "C" __attribute__((visibility("default")))
 
@@ -714,8 +715,17 @@ static int enqueue(const Model* m, const Replica* rep, ExecCtx* c, const float* 
               return ST_DEVICE;
             }
           }
-          if (tc_rc == 0) {
-            // launched on the tensor cores
+          // few output columns (small heads): the narrow-N kernel
+          int nrc = 1;
+          if (tc_rc != 0 && !exact && st.N <= kNarrowMaxN) {
+            nrc = launch_narrow_gemm(a.A, a.B, a.bias, a.res, a.Y, M, st.K, st.N, a.epi, sm, s);
+            if (nrc < 0) {
+              set_error(std::string("narrow GEMM launch failed: ") + cudaGetErrorString(cudaGetLastError()));
+              return ST_DEVICE;
+            }
+          }
+          if (tc_rc == 0 || nrc == 0) {
+            // launched on the tensor cores / the narrow-N kernel
           } else if (exact) {
             dispatch_simt<true, false>(a, sm, s);
           } else {

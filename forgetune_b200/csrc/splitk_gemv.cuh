@@ -18,12 +18,27 @@
 // zero again).
 #pragma once
 
+#include <atomic>
 #include <cstdint>
 #include <cuda_runtime.h>
 
 #include "epilogue.cuh"
 
 namespace ftb {
+
+// Raises a kernel's dynamic shared-memory limit to `bytes` once per device
+// (the attribute belongs to the device's context); `done` holds one bit per
+// device and may be shared by threads.
+template <typename Kernel>
+inline bool smem_limit_once(Kernel kernel, int bytes, std::atomic<uint64_t>& done) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return false;
+  const uint64_t bit = 1ull << dev;
+  if (done.load() & bit) return true;
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess) return false;
+  done.fetch_or(bit);
+  return true;
+}
 
 constexpr int kSkCols = 64;     // columns per CTA (two per lane)
 constexpr int kSkWarps = 8;
@@ -163,22 +178,13 @@ inline int launch_splitk(SplitKArgs a, int sm_count, cudaStream_t s) {
   const int mmax = a.M <= 8 ? 8 : 16;
   const size_t smem = (size_t)mmax * kc * 4 + (size_t)kSkWarps * mmax * kSkCols * 4;
   dim3 grid((unsigned)((a.N + kSkCols - 1) / kSkCols), (unsigned)ks);
-  static bool attr8 = false, attr16 = false;
+  // the shared-memory limit is per device context: set once per device
+  static std::atomic<uint64_t> attr8{0}, attr16{0};
   if (mmax == 8) {
-    if (!attr8) {
-      if (cudaFuncSetAttribute(splitk_gemv_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024) !=
-          cudaSuccess)
-        return -1;
-      attr8 = true;
-    }
+    if (!smem_limit_once(splitk_gemv_kernel<8>, 96 * 1024, attr8)) return -1;
     splitk_gemv_kernel<8><<<grid, kSkWarps * 32, smem, s>>>(a);
   } else {
-    if (!attr16) {
-      if (cudaFuncSetAttribute(splitk_gemv_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024) !=
-          cudaSuccess)
-        return -1;
-      attr16 = true;
-    }
+    if (!smem_limit_once(splitk_gemv_kernel<16>, 96 * 1024, attr16)) return -1;
     splitk_gemv_kernel<16><<<grid, kSkWarps * 32, smem, s>>>(a);
   }
   return cudaGetLastError() == cudaSuccess ? 0 : -1;
