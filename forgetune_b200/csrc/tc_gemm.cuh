@@ -113,11 +113,11 @@ inline int64_t tc_padded_k(int64_t K) { return (K + kTcBK - 1) / kTcBK * kTcBK; 
 inline bool tc_gemm_supported(int64_t K, int64_t N) { return K % 4 == 0 && K >= kTcBK && N >= 32; }
 
 // Shape rule of policy `auto` (the autotuner measures instead): on B200 the
-// tensor cores beat the SIMT kernel from a few hundred rows (tuning runs
-// measured 2x at 256 rows for 784x256 and 512x512 layers); below that the
-// split-K / SIMT kernels win.
+// tensor cores beat the SIMT tile kernel from 17 rows on (tuning runs: 2x at
+// 256 rows for 784x256 and 512x512 layers, and a tiny-MLP forward of 17..127
+// rows in 51 us against 110 us); up to 16 rows the split-K GEMV wins.
 inline bool tc_gemm_profitable(int64_t M, int64_t K, int64_t N) {
-  return M >= 128 && N >= 64 && K >= 64;
+  return M > 16 && N >= 64 && K >= 64;
 }
 
 // round-to-nearest, ties away from zero, to the 10-bit tf32 mantissa (what

@@ -101,7 +101,7 @@ def test_run_to_run_and_batch_invariance(policy, tmp_root):
     # that selects the same kernels give the same bits.  "simt_exact" uses one
     # kernel family for every size; "simt" uses the split-K kernel up to 16
     # rows and register tiles (narrow-N kernel for the head) above; "auto"
-    # adds the tensor cores from 128 rows and split-K for few, long-K tiles.
+    # adds the tensor cores from 17 rows and split-K for few, long-K tiles.
     slices = {"simt_exact": ((0, 1), (100, 357), (4096, 8192), (65000, 65536)),
               "simt": ((100, 357), (4096, 8192), (65000, 65536)),
               "auto": (), "tcgen05": ()}[policy]
