@@ -217,6 +217,33 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
       : "memory");
 }
 
+// L2 eviction priorities for TMA traffic: streamed operands read once go
+// first, weights every tile re-reads and outputs the next layer reads stay.
+__device__ __forceinline__ uint64_t l2_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ uint64_t l2_evict_last() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ uint64_t l2_evict_normal() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+__device__ __forceinline__ void tma_load_2d_hint(void* dst, const CUtensorMap* map, int c0, int c1, uint64_t* bar,
+                                                 uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
@@ -381,11 +408,12 @@ __device__ __forceinline__ void epi_group(float (&e)[4], uint32_t epi, const flo
   }
 }
 
-// TMA store of a staged box to (column c0, row c1, slice c2) of the output map
+// TMA store of a staged box to (column c0, row c1, slice c2) of the output
+// map, kept in L2 for its reader (the next layer or the split-K reduction)
 __device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void* src, int c0, int c1, int c2) {
-  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%1, %2, %3}], [%4];" ::"l"(
-                   reinterpret_cast<uint64_t>(map)),
-               "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(src))
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group.L2::cache_hint [%0, {%1, %2, %3}], [%4], %5;" ::
+                   "l"(reinterpret_cast<uint64_t>(map)),
+               "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(src)), "l"(l2_evict_last())
                : "memory");
 }
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
@@ -625,6 +653,11 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
     // TMA producer: the whole warp runs the loop (so the loop state is
     // warp-uniform); one elected lane issues the copies
     if (lane == 0) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_a)) : "memory");
+    // A is read once when one tile spans all of N (evict it first, keeping the
+    // weights and the previous layer's output resident); the weights are
+    // re-read by every tile
+    const uint64_t pol_a = tiles_n == 1 ? l2_evict_first() : l2_evict_normal();
+    const uint64_t pol_w = l2_evict_last();
     uint32_t it = 0;
     bool ok = true;
     for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
@@ -636,9 +669,9 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
         if (!(ok = mbar_wait_warp(&empty[s], (r & 1u) ^ 1u, abort_flag, p.err, 1))) break;
         if (elect_one()) {
           mbar_arrive_expect_tx(&full[s], L::TX_BYTES);
-          tma_load_2d(a_tile(s), &map_a, kb * BK, m0, &full[s]);
-          tma_load_2d(bhi_tile(s), &map_bhi, kb * BK, n0, &full[s]);
-          tma_load_2d(blo_tile(s), &map_blo, kb * BK, n0, &full[s]);
+          tma_load_2d_hint(a_tile(s), &map_a, kb * BK, m0, &full[s], pol_a);
+          tma_load_2d_hint(bhi_tile(s), &map_bhi, kb * BK, n0, &full[s], pol_w);
+          tma_load_2d_hint(blo_tile(s), &map_blo, kb * BK, n0, &full[s], pol_w);
         }
         __syncwarp();
       }

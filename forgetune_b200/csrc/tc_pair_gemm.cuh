@@ -254,6 +254,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
 
   if (warp == 0) {
     if (lane == 0) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_a)) : "memory");
+    // A is read once when one tile spans all of N (evict it first, keeping the
+    // weights and the previous layer's output resident); the weights are
+    // re-read by every tile
+    const uint64_t pol_a = tiles_n == 1 ? l2_evict_first() : l2_evict_normal();
+    const uint64_t pol_w = l2_evict_last();
     uint32_t it = 0;
     bool ok = true;
     for (int u = pair; u < work.units && ok; u += npairs) {
@@ -269,9 +274,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
         if (!(ok = pair_wait_warp(&empty[s], (r & 1u) ^ 1u, abort_flag, peer_abort, p.err, 1))) break;
         if (elect_one()) {
           mbar_arrive_expect_tx(&full[s], L::TX_BYTES);
-          tma_load_2d(a_tile(s), &map_a, kb * BK, m0, &full[s]);
-          tma_load_2d(bhi_tile(s), &map_bhi, kb * BK, nb, &full[s]);
-          tma_load_2d(blo_tile(s), &map_blo, kb * BK, nb, &full[s]);
+          tma_load_2d_hint(a_tile(s), &map_a, kb * BK, m0, &full[s], pol_a);
+          tma_load_2d_hint(bhi_tile(s), &map_bhi, kb * BK, nb, &full[s], pol_w);
+          tma_load_2d_hint(blo_tile(s), &map_blo, kb * BK, nb, &full[s], pol_w);
         }
         __syncwarp();
       }
