@@ -351,7 +351,7 @@ __device__ __forceinline__ TcEpiSmem tc_epi_setup(const TcKernelParams& p, float
   float* head_bb = head_ba + kTcMaxHeadK;                  // bias of the head, [hp]
   e.head_w = head_w;
   e.head_bb = head_bb;
-  e.bias_a = (p.epi & EPI_BIAS_ROWS) ? p.bias : head_ba;
+  e.bias_a = head_ba;  // a column bias; an [M, N] bias is read from global memory
   if (e.hn > 0) {
     const int hn = e.hn, hp = e.hp;
     for (int i = threadIdx.x - 192; i < p.N * hp; i += 128) {
@@ -424,13 +424,15 @@ __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wa
 // outputs y2[m, o] = epi2(sum_n y[m, n] W2[n, o] + b2[o]) accumulated over n
 // in order (the reference's loop order), each y[m, n] finished by the GEMM's
 // epilogue four columns at a time and consumed at once.
-template <int HP4, bool FULL>
+// ROWS: the bias is [M, N] in global memory, else a column bias staged in
+// shared memory (a compile-time choice, so the compiler sees which memory
+// each pointer reads and issues shared-memory loads for the staged operands).
+template <int HP4, bool FULL, bool ROWS>
 __device__ __forceinline__ void head_chunk(float (&acc)[4 * HP4], const uint32_t (&r)[32], const TcKernelParams& p,
                                            const TcEpiSmem& e, int m, int c, int cnt) {
   const uint32_t epi = p.epi;
   const int64_t off = (int64_t)m * p.N + c;
-  // the column bias is staged in shared memory for all 256 columns
-  const float* bsrc = (epi & EPI_BIAS_ROWS) ? p.bias + off : e.bias_a + c;
+  const float* bsrc = ROWS ? p.bias + off : e.bias_a + c;
   const bool bvec = FULL && aligned16(bsrc);
   const bool rvec = FULL && aligned16(p.res + off);
   const float4* w4 = reinterpret_cast<const float4*>(e.head_w) + (int64_t)c * HP4;
@@ -473,10 +475,12 @@ __device__ __forceinline__ void tc_head_rows(const TcKernelParams& p, const TcEp
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
     const int cnt = min(32, p.N - c);
     if (m < p.M) {
-      if (cnt == 32)
-        head_chunk<HP4, true>(acc, r, p, e, m, c, cnt);
+      if (p.epi & EPI_BIAS_ROWS)
+        head_chunk<HP4, false, true>(acc, r, p, e, m, c, cnt);
+      else if (cnt == 32)
+        head_chunk<HP4, true, false>(acc, r, p, e, m, c, cnt);
       else
-        head_chunk<HP4, false>(acc, r, p, e, m, c, cnt);
+        head_chunk<HP4, false, false>(acc, r, p, e, m, c, cnt);
     }
   }
   if (m < p.M) {
@@ -597,7 +601,10 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
   constexpr int BMT = kTcBM * MH;          // rows per tile
   constexpr uint32_t TMEM_COLS = 2 * MH * BN;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // aligned by pointer arithmetic on the shared array (not through an
+  // integer), so every pointer derived from it stays a shared-memory pointer
+  // to the compiler: ld.shared / st.shared rather than generic accesses
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   auto a_tile = [&](int s) { return reinterpret_cast<float*>(smem + s * L::STAGE_BYTES); };
   auto alo_tile = [&](int s) { return reinterpret_cast<float*>(smem + s * L::STAGE_BYTES + L::A_BYTES); };
   auto bhi_tile = [&](int s) { return smem + s * L::STAGE_BYTES + 2 * L::A_BYTES; };
