@@ -24,6 +24,8 @@
 //              also orders this CTA's W half before the MMAs;
 //   warps 6-9  epilogue of this CTA's 128 rows, then arrive on the leader's
 //              accumulator-free barrier (8 arrivals).
+// The accumulators take all of TMEM: two buffers of 256 columns or four of
+// 128, so at BN=128 a slow epilogue delays the MMAs only three tiles later.
 // Waits are bounded as in the one-SM kernel; a CTA that gives up also raises
 // its peer's abort flag.  Both CTAs meet at a cluster barrier before TMEM is
 // released, so neither leaves while MMAs of the pair may still touch its
@@ -170,7 +172,8 @@ struct TcPairSmem {
   static constexpr int TX_BYTES = A_BYTES + 2 * B_BYTES;
   static constexpr int EPI_BYTES = 4 * 32 * 33 * 4;
   static constexpr int HEAD_BYTES = (kTcMaxHeadK * kTcMaxHeadN + kTcMaxHeadK + kTcMaxHeadN) * 4;
-  static constexpr int NBAR = 3 * STAGES + 6;
+  static constexpr int NACC = 512 / BN;  // accumulator buffers: all of TMEM (2 of 256 or 4 of 128 columns)
+  static constexpr int NBAR = 3 * STAGES + 2 * NACC + 2;
   static constexpr int BAR_BYTES = 8 * NBAR + 16;
   static constexpr int TOTAL = 1024 + STAGES * STAGE_BYTES + EPI_BYTES + HEAD_BYTES + BAR_BYTES;
 };
@@ -183,7 +186,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
   using L = TcPairSmem<BN, BK, STAGES>;
   static_assert(L::TOTAL <= 227 * 1024, "shared memory budget");
   static_assert(BN == 128 || BN == 256, "W^T tiles split into two halves of 64 or 128 rows");
-  constexpr uint32_t TMEM_COLS = 2 * BN;
+  constexpr uint32_t NACC = L::NACC;
+  constexpr uint32_t TMEM_COLS = NACC * BN;
   extern __shared__ uint8_t smem_raw[];
   // the same offsets in both CTAs: the pair's MMAs address the peer's tiles
   // through the leader's descriptors
@@ -201,9 +205,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
   uint64_t* full = bars;                // this CTA's TMA landed
   uint64_t* conv = bars + STAGES;       // leader: A of both CTAs split (8 arrivals)
   uint64_t* empty = bars + 2 * STAGES;  // the pair's MMAs done reading the stage
-  uint64_t* accf = bars + 3 * STAGES;   // [2] accumulator buffer complete
-  uint64_t* acce = accf + 2;            // [2] leader: buffer drained by both epilogues (8 arrivals)
-  uint64_t* drain = acce + 2;           // leader: MMAs retired after an abort
+  uint64_t* accf = bars + 3 * STAGES;   // [NACC] accumulator buffer complete
+  uint64_t* acce = accf + NACC;         // [NACC] leader: buffer drained by both epilogues (8 arrivals)
+  uint64_t* drain = acce + NACC;        // leader: MMAs retired after an abort
   uint64_t* never = drain + 1;          // never arrived on (stall_test)
   volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(never + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(never + 1) + 1;
@@ -233,7 +237,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
       mbar_init(&conv[s], 8);
       mbar_init(&empty[s], 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < (int)NACC; ++b) {
       mbar_init(&accf[b], 1);
       mbar_init(&acce[b], 8);
     }
@@ -293,7 +297,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
         int m0, n0, width, kb0, kb1, slice;
         work.unit(u, BN, m0, n0, width, kb0, kb1, slice);
         const uint32_t idesc = idesc_tf32_pair(width);
-        const uint32_t buf = tc & 1u, use = tc >> 1;
+        const uint32_t buf = tc % NACC, use = tc / NACC;
         if (!(ok = pair_wait_warp(&acce[buf], (use & 1u) ^ 1u, abort_flag, peer_abort, p.err, 2))) break;
         tc_fence_after();
         const uint32_t d = tmem + buf * (uint32_t)BN;
@@ -359,10 +363,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
   } else {
     // warps 6..9: epilogue of this CTA's 128 rows, one TMEM lane quarter each
     const int q = warp & 3;
+    if (lane == 0 && p.y_tma)
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_y)) : "memory");
     const TcEpiSmem e = tc_epi_setup(p, epi_stage, warp - 6, head_smem);
     uint32_t tc = 0;
     for (int u = pair; u < work.units; u += npairs, ++tc) {
-      const uint32_t buf = tc & 1u, use = tc >> 1;
+      const uint32_t buf = tc % NACC, use = tc / NACC;
       if (!pair_wait_warp(&accf[buf], use & 1u, abort_flag, peer_abort, p.err, 7)) break;
       tc_fence_after();
       int m0, n0, width, kb0, kb1, slice;
