@@ -184,6 +184,10 @@ class EngineModel:
             self._check(rc, "profile_read")
         return [float(buf[i]) for i in range(n)]
 
+    def graph_kernels(self) -> int:
+        """Kernels one replay of the most recently captured launch-list graph launches."""
+        return int(lib().ftb_model_counter(self.handle, 4))
+
     def close(self) -> None:
         if self.handle:
             lib().ftb_model_destroy(self.handle)

@@ -154,6 +154,7 @@ struct Model {
   std::vector<ExecCtx*> all_ctxs;
   std::mutex mu;
   std::atomic<size_t> process_allocs{0};
+  std::atomic<size_t> graph_kernels{0};  // kernel nodes of the most recently captured launch-list graph
   bool allow_tc = true;
   std::atomic<int> tc_stall_test{0};  // failure-detection hook, see ftb_model_set_fault_injection
 };
@@ -827,6 +828,19 @@ static int run_graph(Model* m, Replica* rep, ExecCtx* c, const float* in, float*
     set_error(std::string("graph capture failed: ") + cudaGetErrorString(e));
     return ST_DEVICE;
   }
+  {
+    // kernels one replay launches (the step list minus fused-away steps,
+    // plus the extra passes of split-K and convolutions)
+    size_t n = 0, k = 0;
+    cudaGraphGetNodes(graph, nullptr, &n);
+    std::vector<cudaGraphNode_t> nodes(n);
+    if (n && cudaGraphGetNodes(graph, nodes.data(), &n) == cudaSuccess)
+      for (cudaGraphNode_t node : nodes) {
+        cudaGraphNodeType t;
+        if (cudaGraphNodeGetType(node, &t) == cudaSuccess && t == cudaGraphNodeTypeKernel) ++k;
+      }
+    m->graph_kernels.store(k);
+  }
   cudaGraphExec_t exec = nullptr;
   e = cudaGraphInstantiate(&exec, graph, 0);
   cudaGraphDestroy(graph);
@@ -1309,6 +1323,7 @@ FTB_API size_t ftb_model_counter(void* handle, int which) {
   auto* m = static_cast<Model*>(handle);
   if (!m) return 0;
   if (which == 3) return m->process_allocs.load();
+  if (which == 4) return m->graph_kernels.load();
   size_t payload = 0, ins = 0;
   for (auto& kv : t_pools.pools)
     if (kv.first.uid == m->uid) {

@@ -39,6 +39,7 @@
 #include <atomic>
 #include <cstdint>
 #include <cstring>
+#include <utility>
 
 #include "epilogue.cuh"
 
@@ -55,6 +56,23 @@ struct TcWeights {
 
 // Small-N head computed in the epilogue: y2[m, :] = epi2(y[m, :] W2 + b2),
 // with y never stored (W2 is [N, head_n] row-major, head_n <= 16).
+// Launch with programmatic stream serialization (see grid_dep_wait).
+template <typename... KArgs, typename... Args>
+inline cudaError_t pdl_launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                              Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
 struct TcHead {
   const float* w = nullptr;
   const float* bias = nullptr;
@@ -137,6 +155,16 @@ inline float tf32_round_host(float v) {
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
+
+// Programmatic dependent launch.  A kernel launched by pdl_launch may be
+// scheduled while the previous kernel in the stream is still finishing: it
+// sets up its barriers and TMEM, then grid_dep_wait() returns once that
+// kernel has completed and its writes are visible; no global memory is read
+// or written before it.  grid_dep_trigger() lets the next such kernel be
+// scheduled (its CTAs take SMs as this kernel's CTAs exit).  Without the
+// launch attribute both are no-ops.
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dep_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
@@ -654,6 +682,8 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  grid_dep_wait();
+  grid_dep_trigger();
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
@@ -922,9 +952,10 @@ inline int launch_tc_bn(const TcArgs& t, const TcWeights& w, int* err, int sm_co
   const unsigned grid = (unsigned)std::min<int64_t>(ntiles, sm_count);
   const int bi = tc_bn_index(BN);
   const int ki = BK == 32 ? 0 : 1;
-  tc_gemm_kernel<BN, BK, STAGES, MH><<<grid, kTcThreads, L::TOTAL, s>>>(map_a, w.map_hi[ki][bi], w.map_lo[ki][bi],
-                                                                         map_y, p);
-  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+  return pdl_launch(tc_gemm_kernel<BN, BK, STAGES, MH>, dim3(grid), dim3(kTcThreads), L::TOTAL, s, map_a,
+                    w.map_hi[ki][bi], w.map_lo[ki][bi], map_y, p) == cudaSuccess
+             ? 0
+             : -1;
 }
 
 inline int tc_choose_bn(int64_t M, int64_t N, int sm_count, bool head) {

@@ -256,6 +256,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
   tc_fence_before();
   cluster_sync_all();  // both CTAs' barriers initialised and TMEM allocated before any remote arrival
   tc_fence_after();
+  grid_dep_wait();
+  grid_dep_trigger();
   const uint32_t tmem = *tmem_slot;
   const uint32_t peer_abort = cluster_addr(const_cast<int*>(abort_flag), peer);
 
@@ -475,10 +477,10 @@ inline int launch_tc_pair_bn(const TcArgs& t, const TcWeights& w, int* err, cuda
         p.split = 1;
         p.split_from = (int)ntiles;
         const unsigned pairs = (unsigned)std::min<int64_t>(ntiles * S, max_pairs);
-        tc_pair_gemm_kernel<BN, BK, STAGES><<<2 * pairs, kTcThreads, L::TOTAL, s>>>(
-            map_a, w.map_hi[tc_bk_index(BK)][tc_bn_index(BN / 2)], w.map_lo[tc_bk_index(BK)][tc_bn_index(BN / 2)],
-            map_ws, p);
-        if (cudaGetLastError() != cudaSuccess) return -1;
+        if (pdl_launch(tc_pair_gemm_kernel<BN, BK, STAGES>, dim3(2 * pairs), dim3(kTcThreads), L::TOTAL, s, map_a,
+                       w.map_hi[tc_bk_index(BK)][tc_bn_index(BN / 2)],
+                       w.map_lo[tc_bk_index(BK)][tc_bn_index(BN / 2)], map_ws, p) != cudaSuccess)
+          return -1;
         const int64_t quads = t.M * (t.N / 4);
         const int grid = (int)std::min<int64_t>(std::max<int64_t>((quads + 255) / 256, 1), (int64_t)max_pairs * 16);
         tc_splitk_reduce_kernel<<<grid, 256, 0, s>>>(t.ws, S, (int)t.M, (int)t.N, p.epi, p.bias, p.res, p.Y);
@@ -505,9 +507,10 @@ inline int launch_tc_pair_bn(const TcArgs& t, const TcWeights& w, int* err, cuda
   // W^T maps with boxes of BN/2 rows: each CTA loads its half
   const int bi = tc_bn_index(BN / 2);
   const int ki = BK == 32 ? 0 : 1;
-  tc_pair_gemm_kernel<BN, BK, STAGES><<<2 * pairs, kTcThreads, L::TOTAL, s>>>(map_a, w.map_hi[ki][bi],
-                                                                            w.map_lo[ki][bi], map_y, p);
-  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+  return pdl_launch(tc_pair_gemm_kernel<BN, BK, STAGES>, dim3(2 * pairs), dim3(kTcThreads), L::TOTAL, s, map_a,
+                    w.map_hi[ki][bi], w.map_lo[ki][bi], map_y, p) == cudaSuccess
+             ? 0
+             : -1;
 }
 
 // Tile configuration of one tensor-core launch: tile width BN and k-block BK.

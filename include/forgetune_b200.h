@@ -168,7 +168,8 @@ FORGETUNE_EXPORT double ftb_model_benchmark(void* model, const float* input, siz
                                             size_t output_count, int iters);
 FORGETUNE_EXPORT int ftb_model_is_dynamic(void* model);
 FORGETUNE_EXPORT int64_t ftb_model_max_batch(void* model);
-/* which: 0 = payload + insertions, 1 = payload, 2 = insertions, 3 = process total */
+/* which: 0 = payload + insertions, 1 = payload, 2 = insertions, 3 = process total,
+ * 4 = kernels launched by one replay of the most recently captured graph */
 FORGETUNE_EXPORT size_t ftb_model_counter(void* model, int which);
 FORGETUNE_EXPORT void ftb_model_reset_counters(void* model);
 FORGETUNE_EXPORT void ftb_model_inject_alloc(void* model);
