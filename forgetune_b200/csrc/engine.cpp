@@ -87,8 +87,8 @@ std::string check_tune_record(const TuneRecord& r) {
   if (!(r.bn == 0 || r.bn == 64 || r.bn == 128 || r.bn == 256)) return "tile width must be 0, 64, 128 or 256";
   if (!(r.bk == 0 || r.bk == 16 || r.bk == 32)) return "k-block must be 0, 16 or 32";
   if (r.mh < 0 || r.mh > 2) return "row halves must be 0, 1 or 2";
-  if (r.pair < 0 || r.pair > 3) return "pair must be 0, 1, 2 or 3";
-  if (r.pair >= 2 && (r.mh == 2 || (r.bn != 0 && r.bn < 128))) return "SM-pair tiles need width 0, 128 or 256 and row halves 0 or 1";
+  if (r.pair < 0 || r.pair > 4) return "pair must be 0, 1, 2, 3 or 4";
+  if (r.pair >= 2 && r.pair <= 3 && (r.mh == 2 || (r.bn != 0 && r.bn < 128))) return "SM-pair tiles need width 0, 128 or 256 and row halves 0 or 1";
   return "";
 }
 
@@ -589,6 +589,23 @@ Program build_program(const void* blob, size_t bytes) {
     a.head_step = static_cast<int32_t>(i + 1);
     b.head_of = static_cast<int32_t>(i);
   }
+  // two consecutive Linear layers one kernel may compute together
+  for (size_t i = 0; i + 1 < prog.steps.size(); ++i) {
+    Step& a = prog.steps[i];
+    Step& b = prog.steps[i + 1];
+    if (a.kind != ST_GEMM || b.kind != ST_GEMM || a.static_rows || b.static_rows) continue;
+    if (a.mlp_of >= 0 || a.head_of >= 0) continue;  // a is already absorbed by its predecessor
+    if (a.out.space != SP_ARENA || b.a.space != SP_ARENA || b.a.offset != a.out.offset) continue;
+    if (uc.at(static_cast<size_t>(a.node_id)) != 1) continue;
+    if (b.K != a.N || a.N < kMlpMinN1 || a.N > kMlpMaxN1 || b.N < kMlpMinN2 || b.N > kMlpMaxN2) continue;
+    const uint32_t bad = EPI_RESIDUAL | EPI_BIAS_ROWS;
+    if ((a.epi & bad) || (b.epi & bad)) continue;
+    if (a.bias.space != SP_NONE && a.bias.space != SP_WEIGHT) continue;
+    if (b.bias.space != SP_NONE && b.bias.space != SP_WEIGHT) continue;
+    if (b.b.space != SP_WEIGHT || a.b.space != SP_WEIGHT) continue;
+    a.mlp_step = static_cast<int32_t>(i + 1);
+    b.mlp_of = static_cast<int32_t>(i);
+  }
   apply_tuning(prog.steps, g.tuning);
   return prog;
 }
@@ -644,7 +661,8 @@ std::string Program::describe() const {
     os << (i ? "," : "") << "{\"kind\":" << s.kind << ",\"node\":" << s.node_id << ",\"K\":" << s.K
        << ",\"N\":" << s.N << ",\"epi\":" << s.epi << ",\"a\":\"" << space_name(s.a.space) << "\",\"out\":\""
        << space_name(s.out.space) << "\",\"out_offset\":" << s.out.offset << ",\"head_step\":" << s.head_step
-       << ",\"head_of\":" << s.head_of << ",\"tuned\":[";
+       << ",\"head_of\":" << s.head_of << ",\"mlp_step\":" << s.mlp_step << ",\"mlp_of\":" << s.mlp_of
+       << ",\"tuned\":[";
     for (size_t k = 0; k < s.tuned.size(); ++k) {
       const auto& r = s.tuned[k];
       os << (k ? "," : "") << "[" << r.batch_lo << "," << r.batch_hi << "," << r.family << "," << r.bn << "," << r.bk

@@ -204,12 +204,19 @@ struct Step {
   // step can compute it in its epilogue (the intermediate is never stored).
   int32_t head_step = -1;  // index of that step, or -1
   int32_t head_of = -1;    // on the head step: the step that may absorb it
+  // Two-layer fusion: the GEMM step right after this one consumes only this
+  // step's output, 128 < N <= 256 here and 64 <= N <= 128 there, epilogues of
+  // column biases and ReLUs: one kernel may compute both layers (and the
+  // second one's head) with this step's output kept in tensor memory.
+  int32_t mlp_step = -1;   // index of that step, or -1
+  int32_t mlp_of = -1;     // on that step: the step that may absorb it
   // tensor-core tile configuration chosen for this step (0 = by shape), and
   // whether a head may be fused (set by the autotuner or the caller)
   int32_t tc_bn = 0;
   int32_t tc_bk = 0;
   int32_t tc_mh = 0;  // 128-row halves per tile (0 = by shape)
-  int32_t tc_pair = 0;  // 2 = 256-row tiles on an SM pair, 1 = one SM per tile (0 = by shape)
+  int32_t tc_pair = 0;  // 2 = 256-row tiles on an SM pair, 1 = one SM per tile, 3 = pair with split-K,
+                        // 4 = this layer and the next in one kernel (mlp_step); 0 = by shape
   bool fuse_head = true;
   // tuned choices by batch range (GEMM steps); the first matching entry wins
   std::vector<TuneRecord> tuned;
@@ -222,6 +229,7 @@ struct Step {
 
 constexpr int64_t kMaxHeadN = 16;
 constexpr int64_t kMaxHeadK = 256;
+constexpr int64_t kMlpMinN1 = 129, kMlpMaxN1 = 256, kMlpMinN2 = 64, kMlpMaxN2 = 128;
 
 struct Program {
   Graph graph;

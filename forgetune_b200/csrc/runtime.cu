@@ -31,6 +31,7 @@
 #include "simt_gemm.cuh"
 #include "splitk_gemv.cuh"
 #include "tc_pair_gemm.cuh"
+#include "tc_mlp_pair.cuh"
 #include "conv_tc.cuh"
 #include "narrow_gemm.cuh"
 
@@ -598,12 +599,14 @@ static int enqueue(const Model* m, const Replica* rep, ExecCtx* c, const float* 
     }
   };
   const int sm = rep->sm_count;
-  size_t skip_step = (size_t)-1;  // a head step already computed by the previous GEMM's epilogue
+  // steps already computed by an earlier launch: a head fused into the
+  // previous GEMM's epilogue, the second layer of a two-layer kernel and its head
+  size_t skip_step = (size_t)-1, skip_step2 = (size_t)-1;
   for (size_t i = 0; i < rep->steps.size(); ++i) {
     const Step& st = rep->steps[i];
     const int64_t rows = st.static_rows ? 1 : batch;
     if (marks) cudaEventRecord(marks[i], s);
-    if (i == skip_step) continue;
+    if (i == skip_step || i == skip_step2) continue;
     switch (st.kind) {
       case ST_GEMM:
       case ST_CONV: {
@@ -669,6 +672,57 @@ static int enqueue(const Model* m, const Replica* rep, ExecCtx* c, const float* 
             }
             if (rc == 0) break;
           }
+          // this layer and the next in one kernel: by shape when neither step
+          // carries a tile configuration or a tuned entry, or when asked for
+          // (pair 4)
+          if (st.mlp_step >= 0 && !exact && (policy == KP_AUTO || policy == KP_TCGEN05)) {
+            const Step& s2 = rep->steps[(size_t)st.mlp_step];
+            const TcWeights& tw2 = rep->tc[(size_t)st.mlp_step];
+            auto plain = [](const Step& x) { return x.tc_bn == 0 && x.tc_bk == 0 && x.tc_mh == 0 && x.tc_pair == 0; };
+            const TuneRecord* tr2 = s2.tuned_for(batch);
+            const bool asked = (tr ? tr->pair : st.tc_pair) == 4;
+            const bool by_shape = !tr && !tr2 && plain(st) && plain(s2) && tc_gemm_profitable(M, st.K, st.N) &&
+                                  tc_gemm_profitable(M, s2.K, s2.N);
+            if (asked || by_shape) {
+              TcArgs t1{}, t2{};
+              t1.A = a.A;
+              t1.bias = a.bias;
+              t1.M = M;
+              t1.N = st.N;
+              t1.K = st.K;
+              t1.Kp = tw.Kp;
+              t1.epi = st.epi;
+              t1.stall_test = m->tc_stall_test.load();
+              t2.A = nullptr;
+              t2.bias = s2.bias.space ? ptr(s2.bias) : nullptr;
+              t2.Y = ptr(s2.out);
+              t2.M = M;
+              t2.N = s2.N;
+              t2.K = s2.K;
+              t2.Kp = tw2.Kp;
+              t2.epi = s2.epi;
+              const bool head = s2.head_step >= 0 && (tr2 ? tr2->fuse_head : s2.fuse_head);
+              if (head) {
+                const Step& hs = rep->steps[(size_t)s2.head_step];
+                t2.head.w = ptr(hs.b);
+                t2.head.bias = hs.bias.space ? ptr(hs.bias) : nullptr;
+                t2.head.y = ptr(hs.out);
+                t2.head.n = (int)hs.N;
+                t2.head.epi = hs.epi;
+              }
+              const int mrc = launch_tc_mlp(t1, tw, t2, tw2, rep->err_dev, s);
+              if (mrc < 0) {
+                set_error(std::string("two-layer tensor-core launch failed: ") +
+                          cudaGetErrorString(cudaGetLastError()));
+                return ST_DEVICE;
+              }
+              if (mrc == 0) {
+                skip_step = (size_t)st.mlp_step;
+                if (head) skip_step2 = (size_t)s2.head_step;
+                break;
+              }
+            }
+          }
           const bool tc_ok = tw.maps_ready && !exact && fam != TF_SIMT && fam != TF_SPLITK &&
                              (fam == TF_TCGEN05 || policy == KP_TCGEN05 ||
                               (policy == KP_AUTO && tc_gemm_profitable(M, st.K, st.N)));
@@ -694,6 +748,7 @@ static int enqueue(const Model* m, const Replica* rep, ExecCtx* c, const float* 
             cfg.bk = tr ? tr->bk : st.tc_bk;
             cfg.mh = tr ? tr->mh : st.tc_mh;
             cfg.pair = tr ? tr->pair : st.tc_pair;
+            if (cfg.pair == 4) cfg.pair = 0;  // the two-layer kernel did not apply: by shape
             const bool fuse_head = tr ? tr->fuse_head : st.fuse_head;
             if (st.head_step >= 0 && fuse_head) {
               const Step& hs = rep->steps[(size_t)st.head_step];
@@ -1094,11 +1149,11 @@ FTB_API int ftb_model_set_step_config(void* handle, int step, int tc_bn, int tc_
     return ST_CONFIG;
   }
   if (!(tc_bn == 0 || tc_bn == 64 || tc_bn == 128 || tc_bn == 256) || !(tc_bk == 0 || tc_bk == 16 || tc_bk == 32) ||
-      !(tc_mh >= 0 && tc_mh <= 2) || !(tc_pair >= 0 && tc_pair <= 3)) {
-    set_error("tile width must be 0, 64, 128 or 256, k-block 0, 16 or 32, row halves 0, 1 or 2, pair 0..3");
+      !(tc_mh >= 0 && tc_mh <= 2) || !(tc_pair >= 0 && tc_pair <= 4)) {
+    set_error("tile width must be 0, 64, 128 or 256, k-block 0, 16 or 32, row halves 0, 1 or 2, pair 0..4");
     return ST_CONFIG;
   }
-  if (tc_pair >= 2 && (tc_mh == 2 || (tc_bn != 0 && tc_bn < 128))) {
+  if (tc_pair >= 2 && tc_pair <= 3 && (tc_mh == 2 || (tc_bn != 0 && tc_bn < 128))) {
     set_error("SM-pair tiles are 256 rows by 128 or 256 columns (row halves 0 or 1)");
     return ST_CONFIG;
   }
