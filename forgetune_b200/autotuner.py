@@ -258,9 +258,24 @@ class Autotuner:
         static_batch = int(desc["static_batch"])
         steps = desc["steps"]
         gemms = [i for i, s in enumerate(steps) if s["kind"] == _STEP_GEMM]
-        # a unit: a GEMM step and the head step it may absorb
-        units = [[i] + ([steps[i]["head_step"]] if steps[i]["head_step"] >= 0 else [])
-                 for i in gemms if steps[i]["head_of"] < 0]
+        # a unit: a GEMM step and the steps one launch of it may also compute
+        # -- the head it may absorb, or the next layer (and that layer's head)
+        # of a two-layer kernel -- so that every candidate's cost covers the
+        # same work
+        units = []
+        for i in gemms:
+            st = steps[i]
+            if st["head_of"] >= 0 or st.get("mlp_of", -1) >= 0:
+                continue
+            unit = [i]
+            if st.get("mlp_step", -1) >= 0:
+                j = st["mlp_step"]
+                unit.append(j)
+                if steps[j]["head_step"] >= 0:
+                    unit.append(steps[j]["head_step"])
+            elif st["head_step"] >= 0:
+                unit.append(st["head_step"])
+            units.append(unit)
         eng.set_devices([self.device])
         eng.prepare()
 

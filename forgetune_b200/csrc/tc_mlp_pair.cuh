@@ -45,6 +45,19 @@ namespace ftb {
       "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])                                   \
       : "memory")
 
+// tcgen05.wait::ld for a load into r issued earlier: r is an operand, so the
+// compiler treats the registers as written here (the load fills them
+// asynchronously) and neither reads nor moves them before
+#define FTB_TMEM_WAIT_LD32(r)                                                                                 \
+  asm volatile("tcgen05.wait::ld.sync.aligned;"                                                               \
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]), \
+                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),        \
+                 "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]),      \
+                 "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]),      \
+                 "+r"(r[29]), "+r"(r[30]), "+r"(r[31])                                                          \
+               :                                                                                               \
+               : "memory")
+
 // D[256 x N] (+)= A[256 x 8] B[8 x N] over the SM pair, A (tf32) in the TMEM
 // of both CTAs (lane = row, 8 columns from column a_tmem), B from shared
 // memory.
@@ -56,6 +69,31 @@ __device__ __forceinline__ void umma2_tf32_tmem_a(uint32_t d_tmem, uint32_t a_tm
       "tcgen05.mma.cta_group::2.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
       "r"(a_tmem), "l"(b), "r"(idesc), "r"(acc)
       : "memory");
+}
+
+// One chunk of h (32 columns of a row) from layer 1's accumulator to the
+// tf32 hi / lo parts of layer 2's A operand, for the epilogues this kernel
+// takes (a column bias and / or ReLU, fixed at compile time): per value
+// v = relu(acc + b), hi = tf32(v), lo = tf32(v - hi), the operations of the
+// layer-1 epilogue and the layer-2 converter (ReLU before and after a
+// missing residual is ReLU once).
+template <bool BIAS, bool RELU>
+__device__ __forceinline__ void mlp_split_chunk(const uint32_t (&r)[32], const float* b, uint32_t (&hi)[32],
+                                                uint32_t (&lo)[32]) {
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float4 bb = BIAS ? reinterpret_cast<const float4*>(b)[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+    const float b4[4] = {bb.x, bb.y, bb.z, bb.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      float v = __uint_as_float(r[4 * i + k]);
+      if (BIAS) v = __fadd_rn(v, b4[k]);
+      if (RELU) v = relu_keep_nan(v);
+      const float h = tf32_rna(v);
+      hi[4 * i + k] = __float_as_uint(h);
+      lo[4 * i + k] = __float_as_uint(tf32_rna(v - h));
+    }
+  }
 }
 
 constexpr int kTcMlpN1 = 256;  // layer 1's width: its accumulator is TMEM columns [0, 256)
@@ -313,43 +351,44 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
     for (int i = threadIdx.x - 192; i < kTcMlpN1; i += 128) b1s[i] = (bias1 && i < p1.N) ? p1.bias[i] : 0.0f;
     asm volatile("bar.sync 1, 128;" ::: "memory");
     const uint32_t a2rdy_leader = cluster_addr(&a2rdy[0], 0);
+    // layer 1's epilogue: a column bias and / or ReLU (tc_mlp_supported)
+    const bool ep_bias = (p1.epi & EPI_BIAS_LAST) != 0;
+    const bool ep_relu = (p1.epi & (EPI_RELU_PRE | EPI_RELU_POST)) != 0;
     uint32_t tc = 0, g = 0;
     bool ok = true;
     for (int u = pair; u < tiles && ok; u += npairs, ++tc) {
       const int m0 = u * 256 + (int)rank * kTcBM;
       if (!(ok = pair_wait_warp(accf1, tc & 1u, abort_flag, peer_abort, p1.err, 7))) break;
       tc_fence_after();
+      // chunk c+1 is loaded from TMEM while chunk c's stores complete
+      uint32_t r[32];
+      __syncwarp();
+      FTB_TMEM_LD32(tmem + lanes, r);
+      FTB_TMEM_WAIT_LD32(r);
       for (int c = 0; c < nch; ++c) {
         const uint32_t gc = g + (uint32_t)c, qs = gc & 3u, use = gc >> 2;
+        uint32_t hi[32], lo[32];
+        const float* b = b1s + 32 * c;
+        if (ep_bias && ep_relu) mlp_split_chunk<true, true>(r, b, hi, lo);
+        else if (ep_bias) mlp_split_chunk<true, false>(r, b, hi, lo);
+        else if (ep_relu) mlp_split_chunk<false, true>(r, b, hi, lo);
+        else mlp_split_chunk<false, false>(r, b, hi, lo);
+        __syncwarp();
+        if (c + 1 < nch) FTB_TMEM_LD32(tmem + lanes + (uint32_t)(32 * (c + 1)), r);
+        FTB_TMEM_ST32(tmem + lanes + (uint32_t)(32 * c), hi);
+        // the lo slot is free once the MMAs that read its previous chunk completed
         if (use >= 1) {
           if (!(ok = pair_wait_warp(&lofree[qs], (use - 1) & 1u, abort_flag, peer_abort, p1.err, 8))) break;
           tc_fence_after();
         }
-        uint32_t r[32], hi[32], lo[32];
-        __syncwarp();
-        FTB_TMEM_LD32(tmem + lanes + (uint32_t)(32 * c), r);
-        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          float v[4] = {__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1]), __uint_as_float(r[4 * i + 2]),
-                        __uint_as_float(r[4 * i + 3])};
-          // h exactly as the layer-1 epilogue stores it, then the split the
-          // layer-2 converter applies to it
-          epi_group(v, p1.epi, b1s + 32 * c, true, nullptr, false, i, 32);
-#pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const float h = tf32_rna(v[k]);
-            hi[4 * i + k] = __float_as_uint(h);
-            lo[4 * i + k] = __float_as_uint(tf32_rna(v[k] - h));
-          }
-        }
-        FTB_TMEM_ST32(tmem + lanes + (uint32_t)(32 * c), hi);
         FTB_TMEM_ST32(tmem + lanes + LO + 32u * qs, lo);
         asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive_cluster(a2rdy_leader + 8u * qs);
+        FTB_TMEM_WAIT_LD32(r);
       }
+      FTB_TMEM_WAIT_LD32(r);  // nothing left in flight if the loop gave up
       g += (uint32_t)nch;
       if (!ok) break;
       if (!(ok = pair_wait_warp(accf2, tc & 1u, abort_flag, peer_abort, p1.err, 7))) break;
@@ -400,7 +439,9 @@ inline int tc_mlp_prepare(int* max_pairs) {
 // and ReLUs (no [M, N] bias or residual), both weights in tensor-core layout.
 inline bool tc_mlp_supported(const TcArgs& t1, const TcWeights& w1, const TcArgs& t2, const TcWeights& w2) {
   const uint32_t bad = EPI_BIAS_ROWS | EPI_RESIDUAL;
+  const uint32_t epi1_ok = EPI_BIAS_FIRST | EPI_BIAS_LAST | EPI_RELU_PRE | EPI_RELU_POST;
   if (!w1.maps_ready || !w2.maps_ready) return false;
+  if (t1.epi & ~epi1_ok) return false;
   if (t1.N <= 128 || t1.N > kTcMlpN1 || t2.K != t1.N || t2.N < 1 || t2.N > kTcMlpN2) return false;
   if ((t1.epi & bad) || (t2.epi & bad)) return false;
   if (t2.head.n > 0 && (t2.head.n > kTcMaxHeadN || t2.N > kTcMaxHeadK)) return false;
