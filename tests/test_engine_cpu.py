@@ -223,3 +223,41 @@ def test_reference_native_runtime_binds_artifact(tiny_compiled):
             rt.run(x)
     else:
         np.testing.assert_array_equal(rt.run(x), tiny_compiled.run(x))
+
+
+def _mlp_marks(model, x):
+    steps = _native.describe_blob(blob_of(model, x))["steps"]
+    return [(s["mlp_step"], s["mlp_of"], s["head_step"], s["head_of"]) for s in steps]
+
+
+def test_two_layer_candidates():
+    """Step pairs one launch may compute together (first layer 129..256 wide
+    feeding only the second, 64..128 wide, column biases / ReLUs), and the
+    second layer's small head; everything else stays separate launches."""
+    # the tiny MLP: layers 0 and 1 together, the head (step 2) in layer 1's epilogue
+    assert _mlp_marks(workloads.tiny_mlp(), torch.randn(2, 784)) == [(1, -1, -1, -1), (-1, 0, 2, -1),
+                                                                      (-1, -1, -1, 1)]
+    # second layer too narrow for the pair (it is a head of the first instead)
+    m = nn.Sequential(nn.Linear(64, 256), nn.ReLU(), nn.Linear(256, 10)).eval()
+    assert _mlp_marks(m, torch.randn(2, 64)) == [(-1, -1, 1, -1), (-1, -1, -1, 0)]
+    # first layer too wide for layer 1's TMEM columns, or too narrow to be worth it
+    for n1 in (512, 128):
+        m = nn.Sequential(nn.Linear(64, n1), nn.ReLU(), nn.Linear(n1, 128), nn.ReLU()).eval()
+        assert all(t[0] == -1 and t[1] == -1 for t in _mlp_marks(m, torch.randn(2, 64))), n1
+    # three wide layers: only the first pair (a step is in at most one pair)
+    m = nn.Sequential(nn.Linear(64, 200), nn.ReLU(), nn.Linear(200, 100), nn.ReLU(), nn.Linear(100, 256),
+                      nn.ReLU(), nn.Linear(256, 64)).eval()
+    marks = _mlp_marks(m, torch.randn(2, 64))
+    assert marks[0][0] == 1 and marks[1][1] == 0 and marks[2][0] == 3 and marks[3][1] == 2
+    # a layer with a residual epilogue (and the layer whose output it also
+    # reads) stays a separate launch
+    class Res(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.fc = nn.Linear(256, 256)
+
+        def forward(self, x):
+            return torch.relu(self.fc(x)) + x
+
+    m = nn.Sequential(nn.Linear(64, 256), nn.ReLU(), Res(), nn.Linear(256, 128), nn.ReLU()).eval()
+    assert all(t[0] == -1 and t[1] == -1 for t in _mlp_marks(m, torch.randn(2, 64)))
