@@ -22,6 +22,7 @@ CASES = [
     (300, 100, 200, 64, 0, True, False),      # no head: layer 2's output stored; N1 = 200 (ragged chunk)
     (1000, 256, 144, 100, 7, False, True),    # odd count of layer-2 k-blocks, N2 not a multiple of 16
     (5000, 64, 256, 128, 16, True, True),
+    (777, 96, 160, 70, 0, False, False),      # no head, rows of 70 floats: the transposing store epilogue
 ]
 
 
