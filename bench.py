@@ -1,24 +1,33 @@
 #!/usr/bin/env python3
-"""Throughput of the compiled forward pass: tiny MLP 784-256-128-10 at B=65536 per GPU.
+"""Throughput of the compiled forward pass: tiny MLP 784-256-128-10, global B=65536.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-One process per GPU (torchrun for N > 1).  Each rank holds a weight replica
-and processes its own 65536-row shard of a global batch (weak scaling: the
-batch dimension shards with no collective).  Inputs are seeded N(0,1),
-generated on the device by the counter-based Philox generator keyed by the
-global element index, so a rank's shard does not depend on N.
+One process per GPU (torchrun for N > 1).  The global batch of 65536 rows is
+split into contiguous row blocks, one per rank (strong scaling: 8192 rows per
+GPU at N=8); each rank holds a weight replica and runs its block with no
+collective on the data path.  Inputs are seeded N(0,1), generated on the
+device by the counter-based Philox generator keyed by the global element
+index, so a row's values do not depend on N.
 
-value  device-resident samples/s: K forward passes on inputs already in HBM
-       (205 MB input per pass, larger than the 126 MB L2, so no flush is
-       needed), CUDA events on the launching stream, max over ranks.
+value  device-resident samples/s over the global batch: K forward passes
+       (one CUDA-graph replay each) on inputs already in HBM, each bracketed
+       by CUDA events on the launching stream, with L2 flushed (a 256 MB write
+       then read) before every step outside the events; the sum of the K
+       intervals, max over ranks.
 e2e    the same metric through the public host API (CompiledModel.run, the
-       per-model library's forgetune_run_v2) from pinned host memory, the
-       host<->device copies inside the timed region; wall clock around
-       synchronous calls, max over ranks.
+       per-model library's forgetune_run_v2) on each rank's row block from
+       pinned host memory, host<->device copies inside the timed region; wall
+       clock around the synchronous calls, max over ranks.
+extras (same JSON line) weak scaling (65536 rows per GPU) and the wide MLP
+       (262144 rows split over the GPUs) at every N; at N=1 also the batch
+       sweep B in {1, 8, 64, 128, 4096, 65536} (device time per forward and
+       host-API p50), the residual MLP at B=1024 and the small CNN at B=256
+       with their roofline fractions, and the CPU baseline.
 --impl reference  the reference's own CPU runtime (the generated fused_ikj
-       library built from the reference sources into oracle/_ref/) on all
-       host cores: each step is one B=65536 pass split across threads.
+       library built from the reference sources into oracle/_ref/) on every
+       host core, one pinned thread per core: each step is one B=65536 pass
+       split into contiguous row blocks.
 """
 
 from __future__ import annotations
@@ -27,6 +36,7 @@ import argparse
 import ctypes
 import json
 import os
+import queue
 import statistics
 import subprocess
 import sys
@@ -39,12 +49,14 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, HERE)
 
-METRIC = "samples/sec (tiny MLP 784-256-128-10, B=65536 per GPU)"
+METRIC = "samples/sec (tiny MLP 784-256-128-10, global B=65536 split over the GPUs)"
 UNIT = "samples/s"
 BATCH = 65536
 IN_F, OUT_F = 784, 10
 REF_SO = os.path.join(HERE, "oracle", "_ref", "tiny_mlp_fused_ikj.so")
 WORKLOAD = "tiny_mlp_784_256_128_10_dynamic_batch"
+SWEEP = (1, 8, 64, 128, 4096, 65536)
+WIDE_ROWS = 262144
 
 
 def env_int(name, default):
@@ -54,15 +66,26 @@ def env_int(name, default):
         return default
 
 
-def cpu_threads() -> int:
+def host_cpus() -> list:
     try:
-        return len(os.sched_getaffinity(0))
+        return sorted(os.sched_getaffinity(0))
     except AttributeError:
-        return os.cpu_count() or 1
+        return list(range(os.cpu_count() or 1))
+
+
+def cpu_model() -> str:
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
 
 
 # ---------------------------------------------------------------------------
-# reference CPU runtime (oracle/_ref): all host threads, contiguous row slices
+# reference CPU runtime (oracle/_ref): one pinned worker thread per host CPU
 # ---------------------------------------------------------------------------
 class RefRuntime:
     def __init__(self, path: str):
@@ -71,46 +94,108 @@ class RefRuntime:
         self.fn.argtypes = [ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int64]
         self.fn.restype = ctypes.c_int
 
-    def run_split(self, x: np.ndarray, y: np.ndarray, threads: int) -> None:
-        B = x.shape[0]
-        per = (B + threads - 1) // threads
-        errs = []
+    def run(self, x: np.ndarray, y: np.ndarray) -> None:
+        rc = self.fn(x.ctypes.data, x.size, y.ctypes.data, y.size, x.shape[0])
+        if rc != 0:
+            raise RuntimeError("reference runtime returned %d" % rc)
 
-        def work(r0, r1):
-            rc = self.fn(x[r0:r1].ctypes.data, (r1 - r0) * IN_F, y[r0:r1].ctypes.data, (r1 - r0) * OUT_F, r1 - r0)
-            if rc != 0:
-                errs.append(rc)
 
-        ts = [threading.Thread(target=work, args=(r0, min(B, r0 + per))) for r0 in range(0, B, per)]
-        for t in ts:
+class PinnedPool:
+    """Worker threads, each pinned to one host CPU (sched_setaffinity on the
+    thread itself).  The reference runtime is single-threaded per call and
+    thread-safe (thread-local arenas), so N workers make N concurrent calls;
+    ctypes releases the GIL around each."""
+
+    def __init__(self, cpus):
+        self.cpus = list(cpus)
+        self.jobs = [queue.Queue() for _ in self.cpus]
+        self.done = queue.Queue()
+        self.threads = [threading.Thread(target=self._work, args=(i,), daemon=True) for i in range(len(self.cpus))]
+        for t in self.threads:
             t.start()
-        for t in ts:
-            t.join()
+
+    def _work(self, i):
+        try:
+            os.sched_setaffinity(0, {self.cpus[i]})
+        except (AttributeError, OSError):
+            pass
+        while True:
+            fn = self.jobs[i].get()
+            if fn is None:
+                return
+            try:
+                fn()
+                self.done.put(None)
+            except Exception as e:  # reported to the caller
+                self.done.put(e)
+
+    def run(self, fns) -> None:
+        """fns[i] runs on worker i; returns when all have finished."""
+        for i, fn in enumerate(fns):
+            self.jobs[i].put(fn)
+        errs = [self.done.get() for _ in fns]
+        errs = [e for e in errs if e is not None]
         if errs:
-            raise RuntimeError("reference runtime returned %s" % errs)
+            raise errs[0]
+
+    def close(self):
+        for q in self.jobs:
+            q.put(None)
 
 
-def cpu_baseline(seconds: float = 1.5) -> dict:
-    """Reference runtime on every host thread over a bounded sample of the workload."""
+def split_pass(pool: PinnedPool, ref: RefRuntime, x: np.ndarray, y: np.ndarray) -> None:
+    """One pass over x: contiguous row blocks, one call per worker."""
+    n = len(pool.cpus)
+    per = (x.shape[0] + n - 1) // n
+    fns = []
+    for r0 in range(0, x.shape[0], per):
+        r1 = min(x.shape[0], r0 + per)
+        fns.append(lambda a=r0, b=r1: ref.run(x[a:b], y[a:b]))
+    pool.run(fns)
+
+
+def one_core_rate(ref: RefRuntime, x: np.ndarray, seconds: float) -> float:
+    """Samples/s of one pinned thread calling the reference on 2048-row blocks."""
+    pool = PinnedPool(host_cpus()[:1])
+    rows = 2048
+    y = np.empty((rows, OUT_F), np.float32)
+    xs = np.ascontiguousarray(x[:rows])
+    pool.run([lambda: ref.run(xs, y)])  # warm-up: sizes the thread's arena
+    done, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < seconds:
+        pool.run([lambda: ref.run(xs, y)])
+        done += rows
+    rate = done / (time.perf_counter() - t0)
+    pool.close()
+    return rate
+
+
+def cpu_baseline(passes: int = 4) -> dict:
+    """Reference runtime on a bounded sample of the workload: `passes` full
+    B=65536 passes on all host CPUs (one pinned thread each, contiguous row
+    blocks: the procedure of --impl reference), and one pinned core on
+    2048-row blocks for about 2 s."""
     if not os.path.isfile(REF_SO):
         return {"value": None, "unit": UNIT, "cores": 0, "kind": "reference",
                 "sample": "unavailable: oracle/_ref not built"}
     from forgetune_b200 import workloads
-    threads = cpu_threads()
-    rows = min(BATCH, max(threads * 256, 4096))
-    x = workloads.seeded_input((rows, IN_F)).numpy()
-    y = np.empty((rows, OUT_F), np.float32)
+    cpus = host_cpus()
+    x = workloads.seeded_input((BATCH, IN_F)).numpy()
+    y = np.empty((BATCH, OUT_F), np.float32)
     ref = RefRuntime(REF_SO)
-    ref.run_split(x, y, threads)  # warm-up: sizes every thread's arena
-    done, t0 = 0, time.perf_counter()
-    while time.perf_counter() - t0 < seconds:
-        ref.run_split(x, y, threads)
-        done += rows
+    pool = PinnedPool(cpus)
+    split_pass(pool, ref, x, y)  # warm-up: sizes every thread's arena
+    t0 = time.perf_counter()
+    for _ in range(passes):
+        split_pass(pool, ref, x, y)
     dt = time.perf_counter() - t0
-    return {"value": done / dt, "unit": UNIT, "cores": threads, "kind": "reference",
-            "sample": "%d-row slices of the seeded B=65536 input, %d passes over %.1f s wall "
-                      "(%.0f CPU-seconds), reference fused_ikj runtime, one ctypes call per thread"
-                      % (rows, done // rows, dt, dt * threads)}
+    pool.close()
+    one = one_core_rate(ref, x, 2.0)
+    return {"value": BATCH * passes / dt, "unit": UNIT, "cores": len(cpus), "kind": "reference",
+            "cpu_model": cpu_model(), "one_core": {"value": one, "unit": UNIT, "cores": 1},
+            "sample": "%d full B=65536 passes on %d pinned threads (contiguous row blocks, one ctypes call per "
+                      "thread) in %.2f s; one core: one pinned thread on 2048-row blocks for 2 s; reference "
+                      "fused_ikj runtime built from the reference sources" % (passes, len(cpus), dt)}
 
 
 def run_reference(args) -> int:
@@ -122,26 +207,31 @@ def run_reference(args) -> int:
                                                                 "(python oracle/build_ref.py)"}))
         return 0
     from forgetune_b200 import workloads
-    threads = cpu_threads()
+    cpus = host_cpus()
     x = workloads.seeded_input((BATCH, IN_F)).numpy()
     y = np.empty((BATCH, OUT_F), np.float32)
     ref = RefRuntime(REF_SO)
+    pool = PinnedPool(cpus)
     for _ in range(args.warmup):
-        ref.run_split(x, y, threads)
+        split_pass(pool, ref, x, y)
     times = []
     for _ in range(args.steps):
         t0 = time.perf_counter()
-        ref.run_split(x, y, threads)
+        split_pass(pool, ref, x, y)
         times.append(time.perf_counter() - t0)
+    pool.close()
     total = sum(times)
     value = BATCH * args.steps / total
+    one = one_core_rate(ref, x, 2.0)
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * total / args.steps,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "batch_per_step": BATCH, "threads": threads},
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "reference",
-                         "sample": "full B=65536 pass per step split over %d threads" % threads},
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "global_batch": BATCH, "threads": len(cpus)},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": len(cpus), "kind": "reference",
+                         "cpu_model": cpu_model(), "one_core": {"value": one, "unit": UNIT, "cores": 1},
+                         "sample": "full B=65536 pass per step on %d pinned threads (contiguous row blocks); "
+                                   "one core: one pinned thread on 2048-row blocks for 2 s" % len(cpus)},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line))
@@ -206,9 +296,123 @@ def load_peaks() -> dict:
     return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "_source": "fallback"}
 
 
+def model_flops(model, sample_shape) -> float:
+    """FLOPs of one sample's forward pass: 2 per multiply-add of every Linear
+    and Conv2d (shapes from a CPU forward with hooks)."""
+    import torch
+    total = [0.0]
+
+    def hook(mod, inp, out):
+        if isinstance(mod, torch.nn.Linear):
+            total[0] += 2.0 * mod.in_features * mod.out_features
+        elif isinstance(mod, torch.nn.Conv2d):
+            kh, kw = mod.kernel_size
+            total[0] += 2.0 * out[0].numel() * (mod.in_channels // mod.groups) * kh * kw
+
+    hs = [m.register_forward_hook(hook) for m in model.modules() if isinstance(m, (torch.nn.Linear, torch.nn.Conv2d))]
+    with torch.no_grad():
+        model(torch.zeros((1,) + tuple(sample_shape)))
+    for h in hs:
+        h.remove()
+    return total[0]
+
+
 # ---------------------------------------------------------------------------
 # our arm
 # ---------------------------------------------------------------------------
+class Timer:
+    """Per-step CUDA events on the launching stream with an L2 flush (256 MB
+    written, then read) before each step, outside the events."""
+
+    def __init__(self, dev, stream):
+        import torch
+        self.torch = torch
+        self.stream = stream
+        self.buf = torch.empty(64 << 20, dtype=torch.float32, device=dev)
+        self.sink = torch.empty((), dtype=torch.float32, device=dev)
+
+    def flush(self):
+        self.buf.zero_()
+        self.torch.sum(self.buf, dim=0, out=self.sink)
+
+    def run(self, step, iters):
+        """Durations (ms) of `iters` calls of step(i), each after a flush."""
+        torch = self.torch
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(iters)]
+        for i in range(iters):
+            self.flush()
+            ev[i][0].record(self.stream)
+            step(i)
+            ev[i][1].record(self.stream)
+        torch.cuda.synchronize()
+        return [a.elapsed_time(b) for a, b in ev]
+
+
+def build_engine(model, sample_shape, max_batch, dev_index, policy="auto"):
+    """The compiled graph (the blob compile_model embeds) as an engine handle."""
+    import torch
+    from forgetune_b200 import _native
+    from forgetune_b200.frontend import export_to_ir
+    from forgetune_b200.graph_blob import serialize
+    x = torch.zeros((2,) + tuple(sample_shape))
+    ir = export_to_ir(model, (x,), dynamic_batch=True, max_batch_size=max_batch)
+    eng = _native.EngineModel(serialize(ir, enable_fusion=True, bias_first_fused=True, kernel_policy=policy))
+    eng.set_devices([dev_index])
+    eng.prepare()
+    return eng
+
+
+def forward_profile(eng, step_fn, timer, iters):
+    """Per-launch-list-step device ms averaged over `iters` profiled runs."""
+    for i in range(2):
+        step_fn(i)
+    import torch
+    torch.cuda.synchronize()
+    for i in range(iters):
+        timer.flush()
+        step_fn(i)
+    torch.cuda.synchronize()
+    return np.array([eng.profile_read(i) for i in range(iters)]).mean(axis=0)
+
+
+def config_extra(name, builder, sample_shape, B, dev, stream, timer, peak_tflops, iters=20):
+    """Device time per forward of a workload at batch B (graph replays, L2
+    flushed before each), FLOPs and the roofline fraction of the forward and
+    of its dominant launch."""
+    import torch
+    from forgetune_b200 import _native
+    model = builder()
+    eng = build_engine(model, sample_shape, B, dev.index)
+    n_in = B * int(np.prod(sample_shape))
+    out_f = int(model(torch.zeros((1,) + tuple(sample_shape))).shape[1])
+    x = torch.empty(n_in, dtype=torch.float32, device=dev)
+    y = torch.empty(B * out_f, dtype=torch.float32, device=dev)
+    _native.philox_normal(x.data_ptr(), 1, 0, n_in, stream.cuda_stream)
+
+    def step(i):
+        eng.run_device(x.data_ptr(), n_in, y.data_ptr(), B * out_f, B, stream.cuda_stream)
+
+    for i in range(3):
+        step(i)
+    ms = timer.run(step, iters)
+    prof = forward_profile(eng, lambda i: eng.run_device_profiled(x.data_ptr(), n_in, y.data_ptr(), B * out_f, B,
+                                                                  stream.cuda_stream, i), timer, iters)
+    flops = model_flops(model, sample_shape) * B
+    med = statistics.median(ms)
+    dom = int(np.argmax(prof))
+    st = eng.desc["steps"][dom]
+    res = {"workload": name, "batch": B, "device_ms_median": med, "samples_per_s": B / (med / 1000.0),
+           "flops_per_forward": flops, "tflops": flops / (med / 1000.0) / 1e12,
+           "roofline_frac_forward": flops / (med / 1000.0) / 1e12 / peak_tflops,
+           "kernels_per_forward": eng.graph_kernels(),
+           "dominant_step": {"index": dom, "kind": st.get("kind"), "K": st.get("K"), "N": st.get("N"),
+                             "avg_ms": float(prof[dom]), "share_of_forward": float(prof[dom] / prof.sum())},
+           "per_step_ms": [round(float(v), 5) for v in prof],
+           "l2": "flushed before each forward"}
+    eng.close()
+    return res
+
+
 def run_ours(args) -> int:
     import torch
     import torch.distributed as dist
@@ -225,11 +429,14 @@ def run_ours(args) -> int:
     def max_over_ranks(v: float) -> float:
         return sharding.max_over_ranks(v, dev)
 
-    B = args.batch
+    G = args.batch  # global batch
+    r0, r1 = sharding.shard_rows(G, world, rank)
+    B = r1 - r0  # this rank's rows
     model = workloads.tiny_mlp()
     out_dir = tempfile.mkdtemp(prefix="ftb_bench_r%d_" % rank)
     cm = compile_model(model, (workloads.seeded_input((64, IN_F)),), output_dir=out_dir, autotune=False,
-                       kernel_variant="fused_ikj", enable_fusion=True, dynamic_batch=True, max_batch_size=B,
+                       kernel_variant="fused_ikj", enable_fusion=True, dynamic_batch=True,
+                       max_batch_size=max(B, BATCH),
                        max_workspace_bytes=8 << 30, gpu_kernel=args.policy)
     with open(cm.manifest()["artifacts"]["graph_blob"], "rb") as f:
         eng = _native.EngineModel(f.read())
@@ -238,24 +445,25 @@ def run_ours(args) -> int:
     steps_desc = eng.desc["steps"]
 
     stream = torch.cuda.current_stream(dev)
+    timer = Timer(dev, stream)
     x = torch.empty(B * IN_F, dtype=torch.float32, device=dev)
     y = torch.empty(B * OUT_F, dtype=torch.float32, device=dev)
-    _native.philox_normal(x.data_ptr(), 1, sharding.shard_element_offset(rank, B, IN_F), B * IN_F,
-                          stream.cuda_stream)
+    _native.philox_normal(x.data_ptr(), 1, r0 * IN_F, B * IN_F, stream.cuda_stream)
     torch.cuda.synchronize()
 
-    def step(slot=None):
-        # a step is one replay of the forward's CUDA graph (the path the public
-        # API runs); profiled steps launch the same kernels with an event
-        # before every launch-list step, which costs about 3.5 us per event
-        if slot is None:
-            eng.run_device(x.data_ptr(), B * IN_F, y.data_ptr(), B * OUT_F, B, stream.cuda_stream)
-        else:
-            eng.run_device_profiled(x.data_ptr(), B * IN_F, y.data_ptr(), B * OUT_F, B, stream.cuda_stream, slot)
+    def step(i):
+        # one replay of the forward's CUDA graph (the path the public API runs)
+        eng.run_device(x.data_ptr(), B * IN_F, y.data_ptr(), B * OUT_F, B, stream.cuda_stream)
+
+    def step_prof(i):
+        # the same kernels launched with an event before every launch-list
+        # step (about 3.5 us per event): each kernel's device time
+        eng.run_device_profiled(x.data_ptr(), B * IN_F, y.data_ptr(), B * OUT_F, B, stream.cuda_stream, i % 1024)
 
     for i in range(args.warmup):
-        step()
-        step(i % 1024)
+        timer.flush()
+        step(i)
+        step_prof(i)
     torch.cuda.synchronize()
     launches_per_step = eng.graph_kernels()
     barrier()
@@ -264,29 +472,17 @@ def run_ours(args) -> int:
     time.sleep(0.3)
     torch.cuda.synchronize()
     barrier()
-
-    def timed(profiled):
-        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        ev0.record(stream)
-        for i in range(args.steps):
-            step(i % 1024 if profiled else None)
-        ev1.record(stream)
-        torch.cuda.synchronize()
-        return ev0.elapsed_time(ev1)
-
-    # timed region 1 (the headline): K graph replays, nothing else on the stream
-    ms_local = timed(False)
+    # timed region 1 (the headline): K graph replays
+    ms_steps = timer.run(step, args.steps)
     barrier()
-    # timed region 2 (the roofline): the same K steps with per-step events,
-    # giving each kernel's device time
-    ms_prof_local = timed(True)
+    # timed region 2 (the roofline): the same K steps with per-kernel events
+    prof_steps = timer.run(step_prof, args.steps)
     barrier()
     clk = clocks.stop()
-    ms = max_over_ranks(ms_local)
-    ms_prof = max_over_ranks(ms_prof_local)
-    value = world * B * args.steps / (ms / 1000.0)
+    ms = max_over_ranks(sum(ms_steps))
+    ms_prof = max_over_ranks(sum(prof_steps))
+    value = G * args.steps / (ms / 1000.0)
 
-    # per-step device times from the events recorded inside timed region 2
     nprof = min(args.steps, 1024)
     per_step = np.array([eng.profile_read(i) for i in range(nprof)])
     avg = per_step.mean(axis=0)
@@ -300,14 +496,15 @@ def run_ours(args) -> int:
         if steps_desc[ds["mlp_step"]].get("head_step", -1) >= 0:
             fused_steps.append(steps_desc[ds["mlp_step"]]["head_step"])
     peaks = load_peaks()
-    flops = sum(2.0 * B * steps_desc[i]["K"] * steps_desc[i]["N"] for i in fused_steps)
-    achieved_tflops = flops / (avg[dom] / 1000.0) / 1e12
     tc_peak = peaks["bf16_tflops"] / 6.0  # 3xTF32: three tf32 MMAs at half the bf16 rate
+    flops = sum(2.0 * B * steps_desc[i]["K"] * steps_desc[i]["N"] for i in fused_steps)
+    dom_ms = max_over_ranks(float(avg[dom]))
+    achieved_tflops = flops / (dom_ms / 1000.0) / 1e12
     traffic, kname = None, ds.get("kernel", "")
     tpath = os.path.join(HERE, "profiles", "traffic.json")
     if os.path.isfile(tpath):
         with open(tpath) as f:
-            rec = json.load(f).get(WORKLOAD, {})
+            rec = json.load(f).get(WORKLOAD, {}).get("rows_%d" % B, {})
         traffic = rec.get("dominant_kernel_bytes_per_launch")
         kname = kname or rec.get("dominant_kernel", "")
     roofline = {
@@ -316,19 +513,41 @@ def run_ours(args) -> int:
         "kernel": "steps %s: GEMMs %s, M=%d (%s)" % (
             fused_steps, " + ".join("K=%d N=%d" % (steps_desc[i]["K"], steps_desc[i]["N"]) for i in fused_steps),
             B, kname),
-        "algorithmic_flops_per_launch": flops, "avg_launch_ms": float(avg[dom]),
+        "algorithmic_flops_per_launch": flops, "avg_launch_ms": dom_ms,
         "timed_over": "a second timed region of the same %d steps with CUDA events between launch-list steps "
-                      "(%.4f ms per step there, against %.4f ms per step without the events)"
+                      "(%.4f ms per step there, against %.4f ms per step without the events); max over ranks"
                       % (args.steps, ms_prof / args.steps, ms / args.steps),
         "share_of_forward": float(avg[dom] / avg.sum()),
-        "peak_basis": "fp32-accurate contraction on tensor cores = 3xTF32 = %s bf16 dense / 6 (%.0f / 6)"
+        "peak_basis": "fp32-accurate contraction on tensor cores = 3xTF32 = %s bf16 dense / 6 (%.1f / 6)"
                       % (peaks["_source"], peaks["bf16_tflops"]),
-        "fp32_ffma_nominal_tflops": 148 * 128 * 2 * 1.965e9 / 1e12,
+        "forward_frac": (B * 469504.0 / (ms / args.steps / 1000.0) / 1e12) / tc_peak,
     }
 
-    e2e, p50_b1, dev_b1, base = None, None, None, None
+    extras = {}
+    # weak scaling: 65536 rows on every GPU (a larger global batch as N grows)
+    if world > 1:
+        xw = torch.empty(BATCH * IN_F, dtype=torch.float32, device=dev)
+        yw = torch.empty(BATCH * OUT_F, dtype=torch.float32, device=dev)
+        _native.philox_normal(xw.data_ptr(), 1, rank * BATCH * IN_F, BATCH * IN_F, stream.cuda_stream)
+
+        def step_w(i):
+            eng.run_device(xw.data_ptr(), BATCH * IN_F, yw.data_ptr(), BATCH * OUT_F, BATCH, stream.cuda_stream)
+
+        for i in range(3):
+            step_w(i)
+        barrier()
+        wms = max_over_ranks(sum(timer.run(step_w, args.steps)))
+        extras["weak_scaling"] = {"rows_per_gpu": BATCH, "global_batch": BATCH * world,
+                                  "value": BATCH * world * args.steps / (wms / 1000.0), "unit": UNIT,
+                                  "ms_per_step": wms / args.steps}
+        del xw, yw
+    else:
+        extras["weak_scaling"] = {"rows_per_gpu": BATCH, "global_batch": BATCH, "value": value, "unit": UNIT,
+                                  "ms_per_step": ms / args.steps}
+
+    e2e, base = None, None
     if not args.quick:
-        # end to end through the public host API, pinned host buffers
+        # end to end through the public host API, pinned host buffers, this rank's row block
         xh = torch.empty((B, IN_F), dtype=torch.float32, pin_memory=True)
         xh.copy_(x.view(B, IN_F))
         xh_np = xh.numpy()
@@ -340,36 +559,37 @@ def run_ours(args) -> int:
         for _ in range(args.steps):
             out_host = rt.run(xh_np)
         e2e_s = max_over_ranks(time.perf_counter() - t0)
-        e2e = {"value": world * B * args.steps / e2e_s, "unit": UNIT,
-               "h2d_bytes_per_step": B * IN_F * 4, "d2h_bytes_per_step": int(out_host.nbytes),
+        e2e = {"value": G * args.steps / e2e_s, "unit": UNIT,
+               "h2d_bytes_per_step": G * IN_F * 4, "d2h_bytes_per_step": G * OUT_F * 4,
+               "h2d_bytes_per_step_per_gpu": B * IN_F * 4, "d2h_bytes_per_step_per_gpu": int(out_host.nbytes),
                "ms_per_step": 1000.0 * e2e_s / args.steps}
 
-        # p50 latency at B=1 through the host API (graph replay)
-        x1 = np.ascontiguousarray(xh_np[:1])
-        for _ in range(20):
-            rt.run(x1)
-        lat = []
-        for _ in range(200):
-            t0 = time.perf_counter_ns()
-            rt.run(x1)
-            lat.append((time.perf_counter_ns() - t0) / 1000.0)
-        p50_b1 = statistics.median(lat)
-        dev_b1 = cm.benchmark_kernel(iters=1000, batch_size=1)
-        base = cpu_baseline() if (rank == 0 and world == 1) else None
+        # wide MLP at box scale: 262144 rows split over the GPUs, generated per shard on the device
+        extras["wide_mlp"] = wide_mlp_extra(world, rank, dev, stream, timer, tc_peak, max_over_ranks, barrier)
+
+        if world == 1:
+            extras["sweep"] = sweep_extra(cm, eng, dev, stream, timer, tc_peak)
+            extras["residual_mlp"] = config_extra("residual_mlp_512x10_blocks", workloads.residual_mlp, (512,), 1024,
+                                                  dev, stream, timer, tc_peak)
+            extras["small_cnn"] = config_extra("small_cnn_3x32x32", workloads.small_cnn, (3, 32, 32), 256, dev,
+                                               stream, timer, tc_peak)
+            base = cpu_baseline() if rank == 0 else None
     if rank == 0:
+        b1 = extras.get("sweep", {}).get("1", {})
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": WORKLOAD, "batch_per_gpu": B, "global_batch": B * world,
-                       "kernel_policy": args.policy, "parallelism": "batch shards, weight replica per GPU",
-                       "l2": "input 205 MB per pass > 126 MB L2; no flush"},
+            "config": {"workload": WORKLOAD, "global_batch": G, "rows_per_gpu": B,
+                       "kernel_policy": args.policy, "parallelism": "contiguous row blocks, weight replica per GPU",
+                       "l2": "flushed before every timed step (256 MB written, then read), outside the events"},
             "e2e": e2e,
             "gpu_launches": args.steps * launches_per_step,
             "roofline": roofline,
             "clocks": clk,
-            "latency_b1": {"p50_host_api_us": p50_b1, "device_us": dev_b1},
+            "latency_b1": {"p50_host_api_us": b1.get("host_api_p50_us"), "device_us": b1.get("device_us_median")},
             "per_step_ms": [float(v) for v in avg],
+            "extras": extras,
         }
         if base is not None:
             line["cpu_baseline"] = base
@@ -381,16 +601,85 @@ def run_ours(args) -> int:
     return 0
 
 
+def sweep_extra(cm, eng, dev, stream, timer, tc_peak) -> dict:
+    """Config-2 batch sweep: device time per forward (graph replay, L2 flushed
+    before each, median of 30) and the public host API's p50 (pinned input)."""
+    import torch
+    from forgetune_b200 import _native
+    out = {}
+    xmax = torch.empty(max(SWEEP) * IN_F, dtype=torch.float32, device=dev)
+    ymax = torch.empty(max(SWEEP) * OUT_F, dtype=torch.float32, device=dev)
+    _native.philox_normal(xmax.data_ptr(), 1, 0, max(SWEEP) * IN_F, stream.cuda_stream)
+    xh_all = torch.empty((max(SWEEP), IN_F), dtype=torch.float32, pin_memory=True)
+    xh_all.copy_(xmax.view(-1, IN_F))
+    rt = cm._runtime
+    for b in SWEEP:
+        def step(i, b=b):
+            eng.run_device(xmax.data_ptr(), b * IN_F, ymax.data_ptr(), b * OUT_F, b, stream.cuda_stream)
+        for i in range(3):
+            step(i)
+        ms = timer.run(step, 30)
+        med = statistics.median(ms)
+        xb = xh_all[:b].numpy()
+        calls = 200 if b <= 4096 else 20
+        for _ in range(10):
+            rt.run(xb)
+        lat = []
+        for _ in range(calls):
+            t0 = time.perf_counter_ns()
+            rt.run(xb)
+            lat.append((time.perf_counter_ns() - t0) / 1000.0)
+        p50 = statistics.median(lat)
+        flops = 2.0 * b * (784 * 256 + 256 * 128 + 128 * 10)
+        out[str(b)] = {"device_us_median": med * 1000.0, "samples_per_s_device": b / (med / 1000.0),
+                       "host_api_p50_us": p50, "samples_per_s_host_api": b / (p50 / 1e6),
+                       "roofline_frac": flops / (med / 1000.0) / 1e12 / tc_peak,
+                       "kernels_per_forward": eng.graph_kernels()}
+    return out
+
+
+def wide_mlp_extra(world, rank, dev, stream, timer, tc_peak, max_over_ranks, barrier) -> dict:
+    """Config 5: 262144 rows split over the ranks, each shard generated on the
+    device from the global element index; 1 warm-up + 3 timed forwards."""
+    import torch
+    from forgetune_b200 import _native, sharding, workloads
+    r0, r1 = sharding.shard_rows(WIDE_ROWS, world, rank)
+    B = r1 - r0
+    model = workloads.wide_mlp()
+    eng = build_engine(model, (4096,), B, dev.index)
+    x = torch.empty(B * 4096, dtype=torch.float32, device=dev)
+    y = torch.empty(B * 4096, dtype=torch.float32, device=dev)
+    _native.philox_normal(x.data_ptr(), 1, r0 * 4096, B * 4096, stream.cuda_stream)
+
+    def step(i):
+        eng.run_device(x.data_ptr(), B * 4096, y.data_ptr(), B * 4096, B, stream.cuda_stream)
+
+    step(0)
+    torch.cuda.synchronize()
+    barrier()
+    ms = max_over_ranks(sum(timer.run(step, 3)))
+    flops = 2.0 * WIDE_ROWS * (4096 * 8192 + 8192 * 8192 + 8192 * 4096)
+    tflops = flops * 3 / (ms / 1000.0) / 1e12
+    res = {"workload": "wide_mlp_4096_8192_8192_4096", "global_batch": WIDE_ROWS, "rows_per_gpu": B,
+           "n_gpus": world, "steps": 3, "ms_per_step": ms / 3, "samples_per_s": WIDE_ROWS * 3 / (ms / 1000.0),
+           "tflops_all_gpus": tflops, "roofline_frac_per_gpu": tflops / world / tc_peak,
+           "kernels_per_forward": eng.graph_kernels(), "scaling": "strong"}
+    eng.close()
+    del x, y
+    torch.cuda.empty_cache()
+    return res
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--batch", type=int, default=BATCH)
+    ap.add_argument("--batch", type=int, default=BATCH, help="global batch split over the ranks")
     ap.add_argument("--policy", default="auto", choices=["auto", "simt", "simt_exact", "tcgen05"])
     ap.add_argument("--quick", action="store_true",
-                    help="device-resident timing only (no e2e, latency or CPU baseline), for profiler captures")
+                    help="device-resident timing only (no e2e, extras or CPU baseline), for profiler captures")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -100,14 +100,14 @@ inline int launch_im2col(const float* x, float* col, const ConvGeom& g, int K, i
   const int64_t tiles = (rows + kIm2colRows - 1) / kIm2colRows;
   const int gx = (int)std::min<int64_t>(tiles, std::max<int64_t>(1, (int64_t)sm * 8 / chunks));
   im2col_kernel<<<dim3(gx, chunks), 256, 0, s>>>(x, col, g, K, Kp, (int)rows);
-  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+  return note_launch(cudaGetLastError());
 }
 
 inline int launch_rows_to_nchw(const float* src, float* dst, int64_t imgs, int HoWo, int C, cudaStream_t s) {
   if (imgs > 65535) return -1;
   dim3 grid((unsigned)((HoWo + 31) / 32), (unsigned)((C + 31) / 32), (unsigned)imgs);
   rows_to_nchw_kernel<<<grid, 256, 0, s>>>(src, dst, HoWo, C);
-  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+  return note_launch(cudaGetLastError());
 }
 
 }  // namespace ftb

@@ -2,10 +2,30 @@
 #pragma once
 
 #include <cstdint>
+#include <cuda_runtime.h>
 
 #include "flags.h"
 
 namespace ftb {
+
+// The CUDA status of this thread's most recent launch check.  A launcher that
+// returns -1 after its own cudaGetLastError() has consumed (and cleared) the
+// error keeps it here, so the caller's message can still name it.
+inline cudaError_t& launch_error_slot() {
+  static thread_local cudaError_t e = cudaSuccess;
+  return e;
+}
+inline int note_launch(cudaError_t e) {
+  launch_error_slot() = e;
+  return e == cudaSuccess ? 0 : -1;
+}
+// The error behind the last failed launch: the kept status, else whatever
+// the runtime still holds.
+inline cudaError_t take_launch_error() {
+  const cudaError_t e = launch_error_slot();
+  launch_error_slot() = cudaSuccess;
+  return e != cudaSuccess ? e : cudaGetLastError();
+}
 
 // NaN-keeping ReLU, the reference's (std::isnan(v) || v > 0.0f) ? v : 0.0f
 // (src/codegen.cpp:394, 840); fmaxf would turn NaN into 0.

@@ -128,7 +128,7 @@ inline int launch_narrow_gemm(const float* x, const float* w, const float* bias,
     case 12: narrow_gemm_kernel<12><<<grid, kNarrowWarps * 32, 0, s>>>(x, w, bias, res, y, (int)M, (int)K, (int)N, epi); break;
     default: narrow_gemm_kernel<16><<<grid, kNarrowWarps * 32, 0, s>>>(x, w, bias, res, y, (int)M, (int)K, (int)N, epi); break;
   }
-  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+  return note_launch(cudaGetLastError());
 }
 
 }  // namespace ftb

@@ -633,7 +633,7 @@ static int enqueue(const Model* m, const Replica* rep, ExecCtx* c, const float* 
             tc_rc = run_tc_conv(m, rep, c, st, a, tw, st.static_rows ? st.rows_per_sample : batch, sm, s);
             if (tc_rc < 0) {
               set_error(std::string("tensor-core convolution launch failed: ") +
-                        cudaGetErrorString(cudaGetLastError()));
+                        cudaGetErrorString(take_launch_error()));
               return ST_DEVICE;
             }
           }
@@ -665,9 +665,10 @@ static int enqueue(const Model* m, const Replica* rep, ExecCtx* c, const float* 
             sk.N = (int)st.N;
             sk.K = (int)st.K;
             sk.epi = st.epi;
-            const int rc = launch_splitk(sk, sm, s);
+            cudaError_t lerr = cudaSuccess;
+            const int rc = launch_splitk(sk, sm, s, &lerr);
             if (rc < 0) {
-              set_error(std::string("split-K GEMM launch failed: ") + cudaGetErrorString(cudaGetLastError()));
+              set_error(std::string("split-K GEMM launch failed: ") + cudaGetErrorString(lerr));
               return ST_DEVICE;
             }
             if (rc == 0) break;
@@ -713,7 +714,7 @@ static int enqueue(const Model* m, const Replica* rep, ExecCtx* c, const float* 
               const int mrc = launch_tc_mlp(t1, tw, t2, tw2, rep->err_dev, s);
               if (mrc < 0) {
                 set_error(std::string("two-layer tensor-core launch failed: ") +
-                          cudaGetErrorString(cudaGetLastError()));
+                          cudaGetErrorString(take_launch_error()));
                 return ST_DEVICE;
               }
               if (mrc == 0) {
@@ -767,7 +768,7 @@ static int enqueue(const Model* m, const Replica* rep, ExecCtx* c, const float* 
               skip_step = (size_t)st.head_step;
             }
             if (tc_rc < 0) {
-              set_error(std::string("tensor-core GEMM launch failed: ") + cudaGetErrorString(cudaGetLastError()));
+              set_error(std::string("tensor-core GEMM launch failed: ") + cudaGetErrorString(take_launch_error()));
               return ST_DEVICE;
             }
           }
@@ -776,7 +777,7 @@ static int enqueue(const Model* m, const Replica* rep, ExecCtx* c, const float* 
           if (tc_rc != 0 && !exact && st.N <= kNarrowMaxN) {
             nrc = launch_narrow_gemm(a.A, a.B, a.bias, a.res, a.Y, M, st.K, st.N, a.epi, sm, s);
             if (nrc < 0) {
-              set_error(std::string("narrow GEMM launch failed: ") + cudaGetErrorString(cudaGetLastError()));
+              set_error(std::string("narrow GEMM launch failed: ") + cudaGetErrorString(take_launch_error()));
               return ST_DEVICE;
             }
           }
@@ -1501,13 +1502,15 @@ static void noalloc_setup(int dev, NoAllocDevice* d) {
     return;
   }
   d->scratch = static_cast<NoAllocScratch*>(p);
-  if (cudaDeviceGetAttribute(&d->sm_count, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
-      cudaFuncSetAttribute(splitk_gemv_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024) !=
-          cudaSuccess ||
-      cudaFuncSetAttribute(splitk_gemv_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024) !=
-          cudaSuccess) {
+  e = cudaDeviceGetAttribute(&d->sm_count, cudaDevAttrMultiProcessorCount, dev);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(splitk_gemv_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(splitk_gemv_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
+  if (e != cudaSuccess) {
     d->rc = ST_DEVICE;
-    d->err = std::string("split-K kernel set-up failed: ") + cudaGetErrorString(cudaGetLastError());
+    d->err = std::string("split-K kernel set-up failed: ") + cudaGetErrorString(e);
+    cudaGetLastError();
   }
 }
 }  // namespace ftb
@@ -1562,9 +1565,10 @@ FTB_API int ftb_small_gemm_noalloc(const float* d_x, const float* d_w, const flo
   a.K = (int)k;
   a.epi = ((flags & FTB_SMALL_GEMM_BIAS) ? EPI_BIAS_LAST : 0u) | ((flags & FTB_SMALL_GEMM_RELU) ? EPI_RELU_PRE : 0u) |
           ((flags & FTB_SMALL_GEMM_RESIDUAL) ? EPI_RESIDUAL : 0u);
-  const int rc = launch_splitk(a, d.sm_count, s);
+  cudaError_t lerr = cudaSuccess;
+  const int rc = launch_splitk(a, d.sm_count, s, &lerr);
   if (rc != 0) {
-    set_error(std::string("ftb_small_gemm_noalloc: launch failed: ") + cudaGetErrorString(cudaGetLastError()));
+    set_error(std::string("ftb_small_gemm_noalloc: launch failed: ") + cudaGetErrorString(lerr));
     return ST_DEVICE;
   }
   return ST_OK;

@@ -28,16 +28,19 @@ namespace ftb {
 
 // Raises a kernel's dynamic shared-memory limit to `bytes` once per device
 // (the attribute belongs to the device's context); `done` holds one bit per
-// device and may be shared by threads.
+// device and may be shared by threads.  Returns the CUDA status it saw.
 template <typename Kernel>
-inline bool smem_limit_once(Kernel kernel, int bytes, std::atomic<uint64_t>& done) {
+inline cudaError_t smem_limit_once(Kernel kernel, int bytes, std::atomic<uint64_t>& done) {
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return false;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   const uint64_t bit = 1ull << dev;
-  if (done.load() & bit) return true;
-  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess) return false;
+  if (done.load() & bit) return cudaSuccess;
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess) return e;
   done.fetch_or(bit);
-  return true;
+  return cudaSuccess;
 }
 
 constexpr int kSkCols = 64;     // columns per CTA (two per lane)
@@ -169,7 +172,11 @@ inline size_t splitk_part_floats(int64_t K, int64_t N, int sm_count) {
 
 // Launches the split-K kernel; the caller provides `part` (at least
 // splitk_part_floats floats) and zeroed `tickets` (ceil(N/64) entries).
-inline int launch_splitk(SplitKArgs a, int sm_count, cudaStream_t s) {
+// Returns 0 once launched, 1 when M is outside 1..16 (nothing launched), -1 on
+// a CUDA error, whose status goes to *err (the launch check has already
+// consumed it, so cudaGetLastError() would no longer report it).
+inline int launch_splitk(SplitKArgs a, int sm_count, cudaStream_t s, cudaError_t* err) {
+  *err = cudaSuccess;
   if (a.M <= 0 || a.M > 16) return 1;
   int ks, kc;
   splitk_shape(a.K, a.N, sm_count, &ks, &kc);
@@ -181,13 +188,16 @@ inline int launch_splitk(SplitKArgs a, int sm_count, cudaStream_t s) {
   // the shared-memory limit is per device context: set once per device
   static std::atomic<uint64_t> attr8{0}, attr16{0};
   if (mmax == 8) {
-    if (!smem_limit_once(splitk_gemv_kernel<8>, 96 * 1024, attr8)) return -1;
+    *err = smem_limit_once(splitk_gemv_kernel<8>, 96 * 1024, attr8);
+    if (*err != cudaSuccess) return -1;
     splitk_gemv_kernel<8><<<grid, kSkWarps * 32, smem, s>>>(a);
   } else {
-    if (!smem_limit_once(splitk_gemv_kernel<16>, 96 * 1024, attr16)) return -1;
+    *err = smem_limit_once(splitk_gemv_kernel<16>, 96 * 1024, attr16);
+    if (*err != cudaSuccess) return -1;
     splitk_gemv_kernel<16><<<grid, kSkWarps * 32, smem, s>>>(a);
   }
-  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+  *err = cudaGetLastError();
+  return *err == cudaSuccess ? 0 : -1;
 }
 
 }  // namespace ftb

@@ -488,11 +488,9 @@ inline int launch_tc_mlp(const TcArgs& t1, const TcWeights& w1, const TcArgs& t2
   const int64_t tiles = (t1.M + 255) / 256;
   const unsigned pairs = (unsigned)std::min<int64_t>(tiles, max_pairs);
   // W1^T halves of 128 rows, W2^T halves of 64 rows, k-blocks of 16
-  return pdl_launch(tc_mlp_pair_kernel<STAGES>, dim3(2 * pairs), dim3(kTcThreads), L::TOTAL, s, map_a,
-                    w1.map_hi[1][tc_bn_index(128)], w1.map_lo[1][tc_bn_index(128)], w2.map_hi[1][tc_bn_index(64)],
-                    w2.map_lo[1][tc_bn_index(64)], map_y, p1, p2) == cudaSuccess
-             ? 0
-             : -1;
+  return note_launch(pdl_launch(tc_mlp_pair_kernel<STAGES>, dim3(2 * pairs), dim3(kTcThreads), L::TOTAL, s, map_a,
+                                w1.map_hi[1][tc_bn_index(128)], w1.map_lo[1][tc_bn_index(128)],
+                                w2.map_hi[1][tc_bn_index(64)], w2.map_lo[1][tc_bn_index(64)], map_y, p1, p2));
 }
 
 }  // namespace ftb

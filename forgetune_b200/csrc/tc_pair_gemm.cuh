@@ -484,7 +484,7 @@ inline int launch_tc_pair_bn(const TcArgs& t, const TcWeights& w, int* err, cuda
         const int64_t quads = t.M * (t.N / 4);
         const int grid = (int)std::min<int64_t>(std::max<int64_t>((quads + 255) / 256, 1), (int64_t)max_pairs * 16);
         tc_splitk_reduce_kernel<<<grid, 256, 0, s>>>(t.ws, S, (int)t.M, (int)t.N, p.epi, p.bias, p.res, p.Y);
-        return cudaGetLastError() == cudaSuccess ? 0 : -1;
+        return note_launch(cudaGetLastError());
       }
     }
   }

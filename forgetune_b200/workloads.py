@@ -25,6 +25,8 @@ __all__ = [
     "residual_mlp",
     "small_cnn",
     "wide_mlp",
+    "op_mix",
+    "OpMix",
     "seeded_input",
     "WORKLOADS",
 ]
@@ -85,6 +87,41 @@ def wide_mlp() -> nn.Module:
     ).eval()
 
 
+class OpMix(nn.Module):
+    """Every un-fused node form of the reference's code generator in one
+    small NCHW model (src/codegen.cpp:835-958): a convolution without ReLU,
+    ADD and MUL with a channel operand [C,1,1] on NCHW, ADD with a [1,N] row,
+    MUL with an [N] row, SIGMOID, TANH, MUL and ADD of same-shape tensors,
+    FLATTEN and Linear layers without a fused ReLU.  Input [B, 3, 8, 8]."""
+
+    def __init__(self):
+        super().__init__()
+        self.conv = nn.Conv2d(3, 8, 3, padding=1)
+        self.ch_shift = nn.Parameter(0.1 * torch.randn(8, 1, 1))
+        self.ch_scale = nn.Parameter(0.5 + torch.rand(8, 1, 1))
+        self.fc1 = nn.Linear(512, 64)
+        self.col_scale = nn.Parameter(0.5 + torch.rand(64))
+        self.row_shift = nn.Parameter(0.1 * torch.randn(1, 64))
+        self.fc2 = nn.Linear(64, 64)
+        self.head = nn.Linear(64, 10)
+
+    def forward(self, x):
+        h = self.conv(x) + self.ch_shift
+        h = torch.relu(h * self.ch_scale)
+        h = torch.flatten(h, 1)
+        h = self.fc1(h) * self.col_scale
+        h = h + self.row_shift
+        a = torch.sigmoid(h)
+        b = torch.tanh(self.fc2(h))
+        h = a * b + a
+        return self.head(h)
+
+
+def op_mix() -> nn.Module:
+    torch.manual_seed(0)
+    return OpMix().eval()
+
+
 def seeded_input(shape, seed: int = 1) -> torch.Tensor:
     """N(0,1) float32 CPU tensor drawn from ``Generator().manual_seed(seed)``."""
     g = torch.Generator().manual_seed(seed)
@@ -98,4 +135,6 @@ WORKLOADS = {
     "residual_mlp": (residual_mlp, (512,), 1024),
     "small_cnn": (small_cnn, (3, 32, 32), 256),
     "wide_mlp": (wide_mlp, (4096,), 262144),
+    # op coverage (not a measured workload): the reference's elementwise forms
+    "op_mix": (op_mix, (3, 8, 8), 64),
 }

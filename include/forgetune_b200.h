@@ -203,9 +203,13 @@ FORGETUNE_EXPORT int ftb_philox_normal(float* d_out, uint64_t seed, uint64_t fir
  * not fit (about 16 * n * ceil(k / 512) floats or more) return -2 with a
  * message in ftb_last_error().  Enqueued on `stream` (NULL = legacy default
  * stream) without synchronising.  The first call on a device looks up the
- * scratch array's device address and sets kernel attributes; make that first
- * call before any stream capture.  Every call shares the scratch, so calls
- * that overlap on the GPU race on it; calls ordered on one stream do not. */
+ * scratch array's device address and sets kernel attributes; with CUDA's lazy
+ * module loading (the default) that lookup is also what loads the library's
+ * device code on that device, which allocates device memory (the 4 MiB array
+ * among it).  So make the first call on each device during set-up, outside the
+ * allocation-free region and before any stream capture; later calls allocate
+ * nothing.  Every call shares the scratch, so calls that overlap on the GPU
+ * race on it; calls ordered on one stream do not. */
 #define FTB_SMALL_GEMM_BIAS 1u
 #define FTB_SMALL_GEMM_RELU 2u
 #define FTB_SMALL_GEMM_RESIDUAL 4u

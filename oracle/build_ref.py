@@ -17,7 +17,10 @@ and are the reference runtime used as the CPU baseline and to pin the oracle.
 They are git-ignored but travel with the working tree; the intermediate
 graph.json / kernel.cpp files stay in oracle/_ref/_src/, which does not travel.
 
-Usage: python oracle/build_ref.py [--reference /root/reference] [--only tiny_mlp]
+Usage: python oracle/build_ref.py [--reference DIR] [--only tiny_mlp]
+
+The reference checkout is DIR, else $FORGETUNE_REFERENCE, else /root/reference
+(reference_root() below is the one place the default is named).
 """
 
 from __future__ import annotations
@@ -41,8 +44,14 @@ TARGETS = {
     "tiny_mlp": 65536,
     "residual_mlp": 1024,
     "small_cnn": 256,
+    "op_mix": 512,
 }
 VARIANTS = ("fused_ikj", "naive_ijk")
+
+
+def reference_root() -> str:
+    """The reference checkout: $FORGETUNE_REFERENCE, else the default mount."""
+    return os.environ.get("FORGETUNE_REFERENCE", "/root/reference")
 
 
 def build_engine(ref: str) -> str:
@@ -97,21 +106,26 @@ def build_one(ref: str, engine: str, name: str, max_batch: int) -> None:
 
 def main() -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=None)
     ap.add_argument("--only", default=None)
     args = ap.parse_args()
+    args.reference = args.reference or reference_root()
     if not os.path.isdir(os.path.join(args.reference, "src")):
         print("[build_ref] reference checkout not found at %s; nothing to build" % args.reference)
         return 0
     os.makedirs(OUT, exist_ok=True)
     engine = build_engine(args.reference)
+    mpath = os.path.join(OUT, "manifest.json")
     meta = {}
+    if os.path.isfile(mpath):
+        with open(mpath) as f:
+            meta = json.load(f)
     for name, mb in TARGETS.items():
         if args.only and name != args.only:
             continue
         build_one(args.reference, engine, name, mb)
         meta[name] = {"max_batch": mb, "variants": list(VARIANTS)}
-    with open(os.path.join(OUT, "manifest.json"), "w") as f:
+    with open(mpath, "w") as f:
         json.dump(meta, f, indent=1)
     return 0
 

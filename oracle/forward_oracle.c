@@ -103,6 +103,37 @@ ORA_EXPORT void ora_add_channel(int64_t B, int64_t C, int64_t HW, const float* a
             }
 }
 
+/* Elementwise multiply in the reference's three broadcast forms
+ * (src/codegen.cpp:916-958): same shape, row ([N] or [1,N]) and NCHW channel. */
+ORA_EXPORT void ora_mul(int64_t n, const float* a, const float* b, float* y) {
+    for (int64_t i = 0; i < n; ++i) y[i] = a[i] * b[i];
+}
+
+ORA_EXPORT void ora_mul_row(int64_t M, int64_t N, const float* a, const float* b, float* y) {
+    for (int64_t i = 0; i < M; ++i)
+        for (int64_t j = 0; j < N; ++j) y[i * N + j] = a[i * N + j] * b[j];
+}
+
+ORA_EXPORT void ora_mul_channel(int64_t B, int64_t C, int64_t HW, const float* a,
+                                const float* scale, float* y) {
+    for (int64_t b = 0; b < B; ++b)
+        for (int64_t c = 0; c < C; ++c)
+            for (int64_t i = 0; i < HW; ++i) {
+                int64_t idx = (b * C + c) * HW + i;
+                y[idx] = a[idx] * scale[c];
+            }
+}
+
+/* SIGMOID 1 / (1 + exp(-x)) and TANH with the C library's float functions,
+ * the ones std::exp / std::tanh on a float resolve to (src/codegen.cpp:844-859). */
+ORA_EXPORT void ora_sigmoid(int64_t n, const float* a, float* y) {
+    for (int64_t i = 0; i < n; ++i) y[i] = 1.0f / (1.0f + expf(-a[i]));
+}
+
+ORA_EXPORT void ora_tanh(int64_t n, const float* a, float* y) {
+    for (int64_t i = 0; i < n; ++i) y[i] = tanhf(a[i]);
+}
+
 /* Standalone NaN-keeping ReLU (src/codegen.cpp:835-843). */
 ORA_EXPORT void ora_relu(int64_t n, const float* a, float* y) {
     for (int64_t i = 0; i < n; ++i) y[i] = ora_relu1(a[i]);

@@ -59,6 +59,11 @@ def lib() -> ctypes.CDLL:
         L.ora_add_row.argtypes = [i64, i64, vp, vp, vp]
         L.ora_add_channel.argtypes = [i64, i64, i64, vp, vp, vp]
         L.ora_relu.argtypes = [i64, vp, vp]
+        L.ora_mul.argtypes = [i64, vp, vp, vp]
+        L.ora_mul_row.argtypes = [i64, i64, vp, vp, vp]
+        L.ora_mul_channel.argtypes = [i64, i64, i64, vp, vp, vp]
+        L.ora_sigmoid.argtypes = [i64, vp, vp]
+        L.ora_tanh.argtypes = [i64, vp, vp]
         L.ora_conv2d.argtypes = [i64] * 13 + [vp, vp, vp, ctypes.c_int, vp]
         L.ora_conv2d.restype = ctypes.c_int
         L.ora_philox_blocks.argtypes = [ctypes.c_uint64, ctypes.c_uint64, ctypes.c_uint64, vp]
@@ -131,6 +136,48 @@ def add(a, b) -> np.ndarray:
     return y
 
 
+def _binary(a, b, same, row, channel) -> np.ndarray:
+    a = _f32(a)
+    b = _f32(b)
+    y = np.empty_like(a)
+    if a.shape == b.shape:
+        same(a.size, _p(a), _p(b), _p(y))
+    elif a.ndim == 2 and (b.ndim == 1 or (b.ndim == 2 and b.shape[0] == 1)):
+        row(a.shape[0], a.shape[1], _p(a), _p(b), _p(y))
+    elif a.ndim == 4 and b.size == a.shape[1]:
+        channel(a.shape[0], a.shape[1], a.shape[2] * a.shape[3], _p(a), _p(b), _p(y))
+    else:
+        raise ValueError("unsupported broadcast %s, %s" % (a.shape, b.shape))
+    return y
+
+
+def add_bcast(a, b) -> np.ndarray:
+    """ADD with the larger operand first, any of the reference's three forms
+    (a channel operand may be [C] or [C,1,1])."""
+    L = lib()
+    return _binary(a, b, L.ora_add, L.ora_add_row, L.ora_add_channel)
+
+
+def mul(a, b) -> np.ndarray:
+    """MUL with the larger operand first, in the reference's three forms."""
+    L = lib()
+    return _binary(a, b, L.ora_mul, L.ora_mul_row, L.ora_mul_channel)
+
+
+def sigmoid(a) -> np.ndarray:
+    a = _f32(a)
+    y = np.empty_like(a)
+    lib().ora_sigmoid(a.size, _p(a), _p(y))
+    return y
+
+
+def tanh(a) -> np.ndarray:
+    a = _f32(a)
+    y = np.empty_like(a)
+    lib().ora_tanh(a.size, _p(a), _p(y))
+    return y
+
+
 def relu(a) -> np.ndarray:
     a = _f32(a)
     y = np.empty_like(a)
@@ -176,6 +223,8 @@ def run_model(model, x, variant: str = "fused_ikj", fusion: bool = True) -> np.n
     import torch.nn as nn
 
     fused_order = "bias_first" if variant in ("fused_ikj", "loop_ikj") else "bias_last"
+    if type(model).__name__ == "OpMix":
+        return _run_op_mix(model, _f32(x))
     h = _f32(x)
     mods = _flatten_modules(model)
 
@@ -216,3 +265,26 @@ def run_model(model, x, variant: str = "fused_ikj", fusion: bool = True) -> np.n
         else:
             raise TypeError("oracle: unsupported module %r" % type(m).__name__)
     return h
+
+
+def _run_op_mix(m, x: np.ndarray) -> np.ndarray:
+    """forgetune_b200.workloads.OpMix in the reference's node order.  No
+    MATMUL->ADD->RELU or CONV2D->RELU chain occurs, so nothing fuses
+    (src/fusion.cpp:6-131): every Linear is MATMUL then a bias ADD (bias-last),
+    the convolution carries its own bias (src/codegen.cpp:412-624), and ADD /
+    MUL take the larger operand first (python/forgetune/export_frontend.py:16-45)."""
+    def lin(h, layer):
+        return gemm(h, _f32(layer.weight).T.copy(), layer.bias, relu=False, order="bias_last")
+
+    h = conv2d(x, m.conv.weight, m.conv.bias, m.conv.stride, m.conv.padding, m.conv.dilation, relu=False)
+    h = add_bcast(h, m.ch_shift)
+    h = relu(mul(h, m.ch_scale))
+    h = h.reshape(h.shape[0], -1).copy()
+    h = lin(h, m.fc1)
+    h = mul(h, m.col_scale)
+    h = add_bcast(h, m.row_shift)
+    a = sigmoid(h)
+    b = tanh(lin(h, m.fc2))
+    h = mul(a, b)
+    h = add_bcast(h, a)
+    return lin(h, m.head)

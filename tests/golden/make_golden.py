@@ -40,6 +40,7 @@ VARIANTS = ("fused_ikj", "naive_ijk")
 CASES = [
     ("tiny_mlp", 1, "seeded"),
     ("tiny_mlp", 7, "seeded"),
+    ("tiny_mlp", 8, "seeded"),
     ("tiny_mlp", 64, "seeded"),
     ("tiny_mlp", 128, "seeded"),
     ("tiny_mlp", 4096, "seeded"),
@@ -47,12 +48,22 @@ CASES = [
     ("tiny_mlp", 5, "zeros"),
     ("tiny_mlp", 3, "neg100"),
     ("tiny_mlp", 16, "wide_range"),
+    ("tiny_mlp", 64, "wide_range"),
+    ("tiny_mlp", 4096, "wide_range"),
     ("residual_mlp", 1024, "seeded"),
     ("residual_mlp", 3, "wide_range"),
+    ("residual_mlp", 1024, "wide_range"),
     ("small_cnn", 1, "seeded"),
     ("small_cnn", 256, "seeded"),
     ("small_cnn", 2, "neg100"),
+    ("small_cnn", 256, "wide_range"),
+    ("op_mix", 1, "seeded"),
+    ("op_mix", 64, "seeded"),
+    ("op_mix", 300, "seeded"),
+    ("op_mix", 64, "wide_range"),
 ]
+# input scale of each kind: the wide-range inputs are the seeded draw x 1e3
+INPUT_SCALE = {"seeded": 1.0, "zeros": 1.0, "neg100": 1.0, "wide_range": 1e3}
 FULL_OUTPUT_LIMIT = 4096  # store every row up to this batch, sampled rows beyond
 SAMPLED_ROWS = 256
 
@@ -116,7 +127,7 @@ def reference_plan(name: str) -> dict:
 def main() -> int:
     arrays = {}
     meta = {"torch": torch.__version__, "weights_sha256": {}, "cases": [], "reference_plans": {}}
-    for name in ("tiny_mlp", "residual_mlp", "small_cnn"):
+    for name in ("tiny_mlp", "residual_mlp", "small_cnn", "op_mix"):
         meta["reference_plans"][name] = reference_plan(name)
     models = {}
     for name, B, kind in CASES:
@@ -125,7 +136,7 @@ def main() -> int:
             meta["weights_sha256"][name] = weights_sha(models[name])
         x = make_input(name, B, kind)
         key = "%s_B%d_%s" % (name, B, kind)
-        case = {"key": key, "workload": name, "batch": B, "input": kind,
+        case = {"key": key, "workload": name, "batch": B, "input": kind, "input_scale": INPUT_SCALE[kind],
                 "input_sha256": sha(x), "outputs": {}}
         rows = None if B <= FULL_OUTPUT_LIMIT else sampled_rows(B)
         if rows is not None:

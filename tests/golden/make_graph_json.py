@@ -92,4 +92,6 @@ def main(ref_root):
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
+    from oracle.build_ref import reference_root
+    main(sys.argv[1] if len(sys.argv) > 1 else reference_root())

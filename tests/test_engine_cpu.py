@@ -195,7 +195,12 @@ def test_compile_model_argument_checks(tmp_path):
         compile_model(m, (x,), output_dir=str(tmp_path), autotune=False, gpu_kernel="triton")
 
 
-REFERENCE_PY = "/root/reference/python"
+def _reference_python():
+    from oracle.build_ref import reference_root
+    return os.path.join(reference_root(), "python")
+
+
+REFERENCE_PY = _reference_python()
 
 
 @pytest.mark.skipif(not os.path.isdir(REFERENCE_PY), reason="reference checkout not present")

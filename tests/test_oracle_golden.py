@@ -11,6 +11,7 @@ import os
 
 import numpy as np
 import pytest
+import torch
 
 from forgetune_b200 import workloads
 from oracle import oracle
@@ -78,3 +79,33 @@ def test_philox_normal_moments():
     assert abs(float(z.std()) - 1.0) < 0.01
     # counter-based: any window equals the same slice of a longer draw
     np.testing.assert_array_equal(oracle.philox_normal(1, 1000, 77), z[1000:1077])
+
+
+def _float64_forward(m, x):
+    h = x.astype(np.float64)
+    for layer in m:
+        if isinstance(layer, torch.nn.Linear):
+            h = h @ layer.weight.detach().numpy().astype(np.float64).T + layer.bias.detach().numpy()
+        else:
+            h = np.maximum(h, 0.0)
+    return h
+
+
+def test_plain_tolerance_is_unattainable_at_wide_range():
+    """At inputs x 1e3 the reference's fixed atol=1e-4 is below the rounding
+    noise of fp32 arithmetic itself, so only the reference's own operation
+    order can meet it: the reference's two variants (same k order, bias
+    placed differently) fail allclose(1e-4, 1e-4) against each other on the
+    residual MLP, and the exact float64 result fails it against the reference
+    on the tiny MLP.  Both pass once atol is scaled with the input
+    (atol = 1e-4 x 1e3), the criterion the GPU parity tests apply to the
+    non-exact policies on these inputs."""
+    a = GOLD["residual_mlp_B1024_wide_range__fused_ikj"]
+    b = GOLD["residual_mlp_B1024_wide_range__naive_ijk"]
+    assert not np.allclose(a, b, atol=1e-4, rtol=1e-4)
+    assert np.allclose(a, b, atol=1e-4 * 1e3, rtol=1e-4)
+    x = make_input("tiny_mlp", 4096, "wide_range")
+    exact = _float64_forward(model("tiny_mlp"), x)
+    ref = GOLD["tiny_mlp_B4096_wide_range__fused_ikj"]
+    assert not np.allclose(exact, ref, atol=1e-4, rtol=1e-4)
+    assert np.allclose(exact, ref, atol=1e-4 * 1e3, rtol=1e-4)

