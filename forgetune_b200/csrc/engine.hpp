@@ -198,6 +198,7 @@ struct Step {
   // device weight-layout slots, filled at upload: W[K,N] for SIMT,
   // W^T split into tf32 hi / lo [N,Kp] for the tensor-core path
   uint64_t w_kn = 0, w_nk_hi = 0, w_nk_lo = 0;
+  uint64_t w_nk_f32 = 0;  // fp32 W^T [N, K] for the small-batch chain kernel (0 = none)
   int64_t Kp = 0;  // K padded to the tensor-core k-block
   // Small-N head: the GEMM step right after this one consumes only this
   // step's output and has N <= kMaxHeadN, so a tensor-core launch of this

@@ -1,12 +1,30 @@
 // Fused GEMM / conv epilogue shared by the SIMT and tensor-core kernels.
 #pragma once
 
+#include <atomic>
 #include <cstdint>
 #include <cuda_runtime.h>
 
 #include "flags.h"
 
 namespace ftb {
+
+// Raises a kernel's dynamic shared-memory limit to `bytes` once per device
+// (the attribute belongs to the device's context); `done` holds one bit per
+// device and may be shared by threads.  Returns the CUDA status it saw.
+template <typename Kernel>
+inline cudaError_t smem_limit_once(Kernel kernel, int bytes, std::atomic<uint64_t>& done) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  const uint64_t bit = 1ull << dev;
+  if (done.load() & bit) return cudaSuccess;
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess) return e;
+  done.fetch_or(bit);
+  return cudaSuccess;
+}
 
 // The CUDA status of this thread's most recent launch check.  A launcher that
 // returns -1 after its own cudaGetLastError() has consumed (and cleared) the

@@ -32,6 +32,7 @@
 #include "splitk_gemv.cuh"
 #include "tc_pair_gemm.cuh"
 #include "tc_mlp_pair.cuh"
+#include "chain_gemv.cuh"
 #include "conv_tc.cuh"
 #include "narrow_gemm.cuh"
 
@@ -88,6 +89,10 @@ struct Replica {
   std::vector<ConvGeom> conv;  // per step (valid for ST_CONV)
   std::vector<TcWeights> tc;   // per step (valid when the tensor-core path may run)
   int sm_count = 148;
+  // small-batch chain kernel: grid (0 = the launch list is not a chain of
+  // dense layers it can run) and the widest layer input
+  int chain_grid = 0;
+  int64_t chain_kmax = 0;
   // error word the tensor-core kernel writes when a bounded wait gives up;
   // mapped pinned host memory, so the host reads it without a copy
   int* err_host = nullptr;
@@ -117,12 +122,19 @@ struct ExecCtx {
   // split-K partial sums of the SM-pair tensor-core GEMM
   float* ws_ksplit = nullptr;
   size_t ws_ksplit_floats = 0;
+  // grid-barrier counters of the chain kernel (zero between launches)
+  unsigned long long* chain_bar = nullptr;
   bool in_use = false;
+  // pinned host staging for small host-to-host runs (allocated on first use):
+  // the copies then run inside the forward's CUDA graph
+  float* h_in = nullptr;
+  float* h_out = nullptr;
   struct CachedGraph {
     int64_t batch;
     const float* in;
     float* out;
     cudaGraphExec_t exec;
+    bool staged;  // copies h_in -> in before and out -> h_out after the forward
   };
   std::vector<CachedGraph> graphs;
 };
@@ -173,6 +185,8 @@ static void destroy_ctx(ExecCtx* c) {
   if (c->h2d) cudaStreamDestroy(c->h2d);
   if (c->d2h) cudaStreamDestroy(c->d2h);
   if (c->block) cudaFree(c->block);
+  if (c->h_in) cudaFreeHost(c->h_in);
+  if (c->h_out) cudaFreeHost(c->h_out);
   delete c;
 }
 
@@ -315,6 +329,31 @@ static int make_replica(Model* m, int dev, Replica** out) {
           }
     }
   }
+  // The small-batch chain kernel runs launch lists made only of dense layers
+  // on the batch rows, with K a multiple of 4 (float4 rows) and one input row
+  // fitting its shared memory; it reads an fp32 W^T [N, K] copy.
+  {
+    bool ok = !rep->steps.empty() && rep->steps.size() <= (size_t)kChainMaxLayers;
+    int64_t kmax = 0, nmax = 0;
+    for (const Step& s : rep->steps) {
+      if (!ok) break;
+      ok = s.kind == ST_GEMM && !s.static_rows && s.K >= 4 && s.K % 4 == 0 && s.N >= 1 &&
+           s.K * 4 <= kChainSmemBytes && s.K * s.N <= ((int64_t)1 << 26) && s.b.space == SP_WEIGHT;
+      kmax = std::max(kmax, s.K);
+      nmax = std::max(nmax, s.N);
+    }
+    if (ok) {
+      for (Step& s : rep->steps) {
+        const size_t off = append((size_t)s.N * s.K, 16);
+        const float* w = g.weights.data() + s.b.offset;
+        for (int64_t n = 0; n < s.N; ++n)
+          for (int64_t k = 0; k < s.K; ++k) host[off + n * s.K + k] = w[k * s.N + n];
+        s.w_nk_f32 = off;
+      }
+      rep->chain_kmax = kmax;
+      rep->chain_grid = (int)std::min<int64_t>(rep->sm_count, (nmax + kChainWarps - 1) / kChainWarps);
+    }
+  }
   rep->weight_floats = host.size();
   CUDA_TRY(cudaMalloc(&rep->weights, std::max<size_t>(host.size(), 1) * sizeof(float)));
   CUDA_TRY(cudaMemcpy(rep->weights, host.data(), host.size() * sizeof(float), cudaMemcpyHostToDevice));
@@ -406,7 +445,8 @@ static int layout_block(Model* m, ExecCtx* c, size_t min_bytes, bool* did_alloc)
       if ((st.kind == ST_GEMM && tc_gemm_supported(st.K, st.N)) || conv_tc_candidate(st)) any_tc = true;
   const size_t ks_floats = any_tc ? kKsplitWorkspaceFloats : 0;
   const size_t ks_b = round256(ks_floats * sizeof(float));
-  const size_t need = std::max(arena + in_b + out_b + part_b + tick_b + col_b + cout_b + ks_b, min_bytes);
+  const size_t bar_b = 256;  // chain-kernel barrier counters
+  const size_t need = std::max(arena + in_b + out_b + part_b + tick_b + col_b + cout_b + ks_b + bar_b, min_bytes);
   bool fresh = false;
   if (!c->block || c->block_bytes < need) {
     int rc = alloc_block(c, need);
@@ -429,9 +469,19 @@ static int layout_block(Model* m, ExecCtx* c, size_t min_bytes, bool* did_alloc)
   c->ws_ksplit = ks_floats ? reinterpret_cast<float*>(c->block + arena + in_b + out_b + part_b + tick_b + col_b +
                                                       cout_b)
                            : nullptr;
+  c->chain_bar = reinterpret_cast<unsigned long long*>(c->block + arena + in_b + out_b + part_b + tick_b + col_b +
+                                                        cout_b + ks_b);
   if (fresh && c->ws_tickets) {
     // tickets start at zero; every split-K launch leaves them at zero
     if (cudaMemset(c->ws_tickets, 0, tick_b) != cudaSuccess) {
+      cudaGetLastError();
+      set_error("workspace initialisation failed");
+      return ST_DEVICE;
+    }
+  }
+  if (fresh) {
+    // the chain kernel's counters start at zero; every launch leaves them at zero
+    if (cudaMemset(c->chain_bar, 0, bar_b) != cudaSuccess) {
       cudaGetLastError();
       set_error("workspace initialisation failed");
       return ST_DEVICE;
@@ -599,6 +649,45 @@ static int enqueue(const Model* m, const Replica* rep, ExecCtx* c, const float* 
     }
   };
   const int sm = rep->sm_count;
+  // Small batches of a chain of dense layers: the whole forward pass in one
+  // launch (chain_gemv.cuh), unless a tuned entry picks kernels for this batch.
+  if (!exact && (policy == KP_AUTO || policy == KP_SIMT) && rep->chain_grid > 0 && c->chain_bar && batch >= 1 &&
+      batch <= kChainMaxRows && (size_t)batch * (size_t)rep->chain_kmax * 4 <= (size_t)kChainSmemBytes) {
+    bool take = true;
+    ChainParams p;
+    std::memset(&p, 0, sizeof(p));
+    p.n_layers = (int)rep->steps.size();
+    p.M = (int)batch;
+    p.bar = c->chain_bar;
+    p.err = rep->err_dev;
+    p.stall_test = m->tc_stall_test.load();
+    for (size_t i = 0; i < rep->steps.size() && take; ++i) {
+      const Step& st = rep->steps[i];
+      const TuneRecord* tr = st.tuned_for(batch);
+      if (tr && tr->family != TF_HEURISTIC) take = false;
+      ChainLayer& L = p.layer[i];
+      L.a = ptr(st.a);
+      L.w = rep->weights + st.w_nk_f32;
+      L.bias = (st.bias.space && (st.epi & (EPI_BIAS_FIRST | EPI_BIAS_LAST))) ? ptr(st.bias) : nullptr;
+      L.res = st.res.space ? ptr(st.res) : nullptr;
+      L.y = ptr(st.out);
+      L.K = (int)st.K;
+      L.N = (int)st.N;
+      L.epi = st.epi;
+      if (reinterpret_cast<uintptr_t>(L.a) & 15u) take = false;  // float4 rows
+    }
+    if (take) {
+      if (marks) cudaEventRecord(marks[0], s);
+      const size_t smem = (size_t)batch * (size_t)rep->chain_kmax * 4;
+      if (launch_chain(p, rep->chain_grid, smem, s) != 0) {
+        set_error(std::string("chain kernel launch failed: ") + cudaGetErrorString(take_launch_error()));
+        return ST_DEVICE;
+      }
+      if (marks)
+        for (size_t i = 1; i <= rep->steps.size(); ++i) cudaEventRecord(marks[i], s);
+      return ST_OK;
+    }
+  }
   // steps already computed by an earlier launch: a head fused into the
   // previous GEMM's epilogue, the second layer of a two-layer kernel and its head
   size_t skip_step = (size_t)-1, skip_step2 = (size_t)-1;
@@ -856,7 +945,8 @@ static int enqueue(const Model* m, const Replica* rep, ExecCtx* c, const float* 
 static int check_kernel_error(const Replica* rep) {
   const volatile int* e = rep->err_host;
   if (e && *e != 0) {
-    set_error("tensor-core GEMM aborted: a pipeline wait exceeded its limit (code " + std::to_string(*e) + ")");
+    set_error("kernel aborted: a bounded wait (tensor-core pipeline or grid barrier) exceeded its limit (code " +
+              std::to_string(*e) + ")");
     return ST_DEVICE;
   }
   return ST_OK;
@@ -865,16 +955,30 @@ static int check_kernel_error(const Replica* rep) {
 static constexpr size_t kMaxGraphs = 16;
 
 // Replays the launch list for (batch, in, out) as a cached CUDA graph.
+// With `staged`, the graph also copies in_bytes from the context's pinned
+// input staging to `in` first and out_bytes from `out` to the output staging
+// last, so a small host-to-host run is one graph launch.
 static int run_graph(Model* m, Replica* rep, ExecCtx* c, const float* in, float* out, int64_t batch,
-                     cudaStream_t s) {
+                     cudaStream_t s, bool staged = false, size_t in_bytes = 0, size_t out_bytes = 0) {
   for (auto& g : c->graphs)
-    if (g.batch == batch && g.in == in && g.out == out) {
+    if (g.batch == batch && g.in == in && g.out == out && g.staged == staged) {
       CUDA_TRY(cudaGraphLaunch(g.exec, s));
       return ST_OK;
     }
   cudaGraph_t graph = nullptr;
   CUDA_TRY(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
-  int rc = enqueue(m, rep, c, in, out, batch, c->stream);
+  int rc = ST_OK;
+  if (staged && cudaMemcpyAsync(const_cast<float*>(in), c->h_in, in_bytes, cudaMemcpyHostToDevice, c->stream) !=
+                    cudaSuccess) {
+    set_error("staged input copy could not be captured");
+    rc = ST_DEVICE;
+  }
+  if (rc == ST_OK) rc = enqueue(m, rep, c, in, out, batch, c->stream);
+  if (rc == ST_OK && staged &&
+      cudaMemcpyAsync(c->h_out, out, out_bytes, cudaMemcpyDeviceToHost, c->stream) != cudaSuccess) {
+    set_error("staged output copy could not be captured");
+    rc = ST_DEVICE;
+  }
   cudaError_t e = cudaStreamEndCapture(c->stream, &graph);
   if (rc) {
     if (graph) cudaGraphDestroy(graph);
@@ -908,7 +1012,7 @@ static int run_graph(Model* m, Replica* rep, ExecCtx* c, const float* in, float*
     cudaGraphExecDestroy(c->graphs.front().exec);
     c->graphs.erase(c->graphs.begin());
   }
-  c->graphs.push_back({batch, in, out, exec});
+  c->graphs.push_back({batch, in, out, exec, staged});
   CUDA_TRY(cudaGraphLaunch(exec, s));
   return ST_OK;
 }
@@ -923,6 +1027,10 @@ static int resolve_devices(Model* m, std::vector<int>* devs) {
   devs->assign(1, d);
   return ST_OK;
 }
+
+// host-to-host runs whose input and output each fit this many bytes go
+// through pinned staging with the copies inside the graph
+static constexpr size_t kHostStageBytes = 256u << 10;
 
 // rows per pipeline chunk so one chunk's input is about 32 MiB
 static int64_t chunk_rows_for(const Program& p, int64_t batch) {
@@ -953,6 +1061,27 @@ static int run_host_one(Model* m, int dev, const float* in, float* out, int64_t 
     const size_t in_b = (size_t)(p.dynamic ? batch : 1) * p.in_static_elems * 4;
     const size_t out_b = (size_t)(p.output_dynamic ? batch : 1) * p.out_static_elems * 4;
     *rep->err_host = 0;  // the previous synchronous run on this replica has finished
+    if (in_b <= kHostStageBytes && out_b <= kHostStageBytes) {
+      // small run: host memcpy into pinned staging, one graph launch that
+      // copies in, computes and copies out, one synchronisation
+      if (!c->h_in) {
+        if (cudaHostAlloc(reinterpret_cast<void**>(&c->h_in), kHostStageBytes, cudaHostAllocDefault) != cudaSuccess ||
+            cudaHostAlloc(reinterpret_cast<void**>(&c->h_out), kHostStageBytes, cudaHostAllocDefault) !=
+                cudaSuccess) {
+          cudaGetLastError();
+          set_error("pinned host staging allocation failed");
+          return ST_ALLOC;
+        }
+      }
+      std::memcpy(c->h_in, in, in_b);
+      rc = run_graph(m, rep, c, c->d_in, c->d_out, batch, c->stream, true, in_b, out_b);
+      if (rc) return rc;
+      CUDA_TRY(cudaStreamSynchronize(c->stream));
+      rc = check_kernel_error(rep);
+      if (rc) return rc;
+      std::memcpy(out, c->h_out, out_b);
+      return ST_OK;
+    }
     CUDA_TRY(cudaMemcpyAsync(c->d_in, in, in_b, cudaMemcpyHostToDevice, c->stream));
     rc = run_graph(m, rep, c, c->d_in, c->d_out, batch, c->stream);
     if (rc) return rc;

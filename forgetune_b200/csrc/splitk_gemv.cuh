@@ -26,23 +26,6 @@
 
 namespace ftb {
 
-// Raises a kernel's dynamic shared-memory limit to `bytes` once per device
-// (the attribute belongs to the device's context); `done` holds one bit per
-// device and may be shared by threads.  Returns the CUDA status it saw.
-template <typename Kernel>
-inline cudaError_t smem_limit_once(Kernel kernel, int bytes, std::atomic<uint64_t>& done) {
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return e;
-  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-  const uint64_t bit = 1ull << dev;
-  if (done.load() & bit) return cudaSuccess;
-  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-  if (e != cudaSuccess) return e;
-  done.fetch_or(bit);
-  return cudaSuccess;
-}
-
 constexpr int kSkCols = 64;     // columns per CTA (two per lane)
 constexpr int kSkWarps = 8;
 constexpr int kSkMaxKc = 512;   // k per slice, bounds the shared x chunk

@@ -1,7 +1,8 @@
 """The narrow-N GEMM (N <= 16 columns, more than 16 rows, non-exact
 policies): every N from 1 to 16 class, K across the 256-row W chunks, both
-bias orders; against the oracle with the reference's tolerance, bitwise run
-to run."""
+bias orders, and both forms -- one warp per 32 rows when the row blocks fill
+the SMs, eight warps splitting K over 32 rows when they do not; against the
+oracle with the reference's tolerance, bitwise run to run."""
 
 import numpy as np
 import pytest
@@ -14,7 +15,8 @@ from oracle import oracle
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("M,K,N", [(17, 7, 1), (1000, 128, 10), (5000, 600, 16), (333, 300, 3), (64, 33, 12)])
+@pytest.mark.parametrize("M,K,N", [(17, 7, 1), (1000, 128, 10), (5000, 600, 16), (333, 300, 3), (64, 33, 12),
+                                   (1024, 512, 10), (256, 128, 10), (40, 4000, 4), (19000, 200, 10)])
 @pytest.mark.parametrize("variant", ["fused_ikj", "naive_ijk"])
 def test_narrow_gemm_matches_oracle(M, K, N, variant, tmp_path):
     torch.manual_seed(M + N)
