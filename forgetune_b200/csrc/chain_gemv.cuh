@@ -9,9 +9,11 @@
 // a cooperative launch) walks the layers; a layer's outputs are complete
 // for every CTA after a grid-wide barrier, so the next layer reads them.
 //
-// Per layer, a warp owns an output column n at a time and reads W's column
-// as the contiguous row n of an fp32 [N, K] copy of the weights (float4
-// loads, every lane's loads in flight together); the CTA stages the layer's
+// At the start every warp prefetches into L2 the weight rows it will read in
+// every layer (they do not depend on the activations), so after a barrier a
+// layer waits on L2, not HBM.  Per layer, a warp owns an output column n at
+// a time and reads W's column as the contiguous row n of an fp32 [N, K] copy
+// of the weights (float4 loads, eight per lane in flight); the CTA stages the layer's
 // input rows [M, K] in shared memory once (L2 loads: the rows were written
 // by other SMs in this launch).  Each lane accumulates its k = 4 lane + 128 i
 // terms for all M rows; the 32 lane sums of a value are added by a butterfly
@@ -104,6 +106,18 @@ __global__ void __launch_bounds__(kChainWarps * 32, 1) chain_gemv_kernel(const _
   const int nw = gridDim.x * kChainWarps;
   const int M = p.M;
   bool ok = !(p.stall_test && blockIdx.x == 0);  // the hook: CTA 0 leaves without arriving
+  // Every layer's weight rows this warp will read, prefetched into L2 now:
+  // they do not depend on the activations, so later layers find them there
+  // instead of waiting on HBM after each barrier.
+  for (int l = 0; l < p.n_layers && ok; ++l) {
+    const ChainLayer& L = p.layer[l];
+    const size_t row_bytes = (size_t)L.K * 4;
+    for (int n = gw; n < L.N; n += nw) {
+      const char* row = reinterpret_cast<const char*>(L.w) + (size_t)n * row_bytes;
+      for (size_t b = (size_t)lane * 128; b < row_bytes; b += 32 * 128)
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(row + b));
+    }
+  }
   for (int l = 0; l < p.n_layers && ok; ++l) {
     const ChainLayer& L = p.layer[l];
     const int K4 = L.K >> 2, N = L.N;
@@ -115,19 +129,31 @@ __global__ void __launch_bounds__(kChainWarps * 32, 1) chain_gemv_kernel(const _
       float acc[kChainMaxRows];
 #pragma unroll
       for (int m = 0; m < kChainMaxRows; ++m) acc[m] = 0.0f;
-#pragma unroll 4
-      for (int k4 = lane; k4 < K4; k4 += 32) {
-        const float4 wv = __ldg(w4 + k4);
+      // eight float4 of the row per lane in flight at once (K <= 1024 in one round)
+      constexpr int WB = 8;
+      for (int kb = 0; kb < K4; kb += 32 * WB) {
+        float4 wv[WB];
 #pragma unroll
-        for (int m = 0; m < kChainMaxRows; ++m) {
-          if (m < M) {
-            const float4 xv = chain_xs[m * K4 + k4];
-            float s = acc[m];
-            s = fmaf(xv.x, wv.x, s);
-            s = fmaf(xv.y, wv.y, s);
-            s = fmaf(xv.z, wv.z, s);
-            s = fmaf(xv.w, wv.w, s);
-            acc[m] = s;
+        for (int j = 0; j < WB; ++j) {
+          const int k4 = kb + 32 * j + lane;
+          wv[j] = k4 < K4 ? __ldg(w4 + k4) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int j = 0; j < WB; ++j) {
+          const int k4 = kb + 32 * j + lane;
+          if (k4 < K4) {
+#pragma unroll
+            for (int m = 0; m < kChainMaxRows; ++m) {
+              if (m < M) {
+                const float4 xv = chain_xs[m * K4 + k4];
+                float s = acc[m];
+                s = fmaf(xv.x, wv[j].x, s);
+                s = fmaf(xv.y, wv[j].y, s);
+                s = fmaf(xv.z, wv[j].z, s);
+                s = fmaf(xv.w, wv[j].w, s);
+                acc[m] = s;
+              }
+            }
           }
         }
       }

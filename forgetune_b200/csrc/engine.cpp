@@ -87,7 +87,7 @@ std::string check_tune_record(const TuneRecord& r) {
   if (!(r.bn == 0 || r.bn == 64 || r.bn == 128 || r.bn == 256)) return "tile width must be 0, 64, 128 or 256";
   if (!(r.bk == 0 || r.bk == 16 || r.bk == 32)) return "k-block must be 0, 16 or 32";
   if (r.mh < 0 || r.mh > 2) return "row halves must be 0, 1 or 2";
-  if (r.pair < 0 || r.pair > 4) return "pair must be 0, 1, 2, 3 or 4";
+  if (r.pair < 0 || r.pair > 5) return "pair must be 0, 1, 2, 3, 4 or 5";
   if (r.pair >= 2 && r.pair <= 3 && (r.mh == 2 || (r.bn != 0 && r.bn < 128))) return "SM-pair tiles need width 0, 128 or 256 and row halves 0 or 1";
   return "";
 }

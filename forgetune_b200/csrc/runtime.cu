@@ -33,7 +33,7 @@
 #include "tc_pair_gemm.cuh"
 #include "tc_mlp_pair.cuh"
 #include "chain_gemv.cuh"
-#include "conv_tc.cuh"
+#include "tc_conv.cuh"
 #include "narrow_gemm.cuh"
 
 #define FTB_API extern "C" __attribute__((visibility("default")))
@@ -115,15 +115,13 @@ struct ExecCtx {
   // split-K workspace inside the block: partial sums and per-column-block tickets
   float* ws_part = nullptr;
   unsigned* ws_tickets = nullptr;
-  // tensor-core convolution: im2col rows and GEMM output for conv_imgs images
-  float* ws_col = nullptr;
-  float* ws_cout = nullptr;
-  int64_t conv_imgs = 0;
   // split-K partial sums of the SM-pair tensor-core GEMM
   float* ws_ksplit = nullptr;
   size_t ws_ksplit_floats = 0;
-  // grid-barrier counters of the chain kernel (zero between launches)
+  // grid-barrier counters of the chain kernel and the two-layer kernel's
+  // team counters (zero between launches)
   unsigned long long* chain_bar = nullptr;
+  unsigned* team_flags = nullptr;
   bool in_use = false;
   // pinned host staging for small host-to-host runs (allocated on first use):
   // the copies then run inside the forward's CUDA graph
@@ -225,17 +223,13 @@ static thread_local ThreadPools t_pools;
 
 static ThreadPool& pool_of(Model* m, int dev) { return t_pools.pools[PoolKey{m->uid, dev}]; }
 
-// A convolution the tensor-core path can run: its im2col GEMM has N = Cout
-// >= 32 output columns, and its epilogue is per output channel (a residual
-// or [M, N] bias would be indexed in NCHW, which the GEMM rows are not).
+// A convolution the tensor-core path (tc_conv.cuh) runs: N = Cout >= 32
+// output channels and an epilogue of a per-channel bias and ReLUs.
 static bool conv_tc_candidate(const Step& s) {
   return s.kind == ST_CONV && s.N >= 32 && !(s.epi & (EPI_RESIDUAL | EPI_BIAS_ROWS)) &&
          tc_gemm_supported(tc_padded_k(s.K), s.N);
 }
 
-// Workspace budget of the tensor-core convolution per context: the images of
-// one chunk, im2col rows plus GEMM output.
-static constexpr size_t kConvWorkspaceBytes = 256u << 20;
 // Split-K partial sums per context (see launch_tc_pair_bn): 74 pairs x 256
 // rows x 256 columns of fp32 covers every split it chooses on a B200.
 static constexpr size_t kKsplitWorkspaceFloats = (size_t)74 * 256 * 256;
@@ -420,23 +414,6 @@ static int layout_block(Model* m, ExecCtx* c, size_t min_bytes, bool* did_alloc)
     if (st.kind == ST_GEMM) max_n = std::max(max_n, st.N);
   const size_t part_b = round256((size_t)kSkMaxSlices * 16 * (size_t)max_n * sizeof(float));
   const size_t tick_b = round256((size_t)((max_n + kSkCols - 1) / kSkCols + 1) * sizeof(unsigned));
-  // tensor-core convolution: one chunk of images, sized for the largest step
-  size_t img_col = 0, img_out = 0;
-  int64_t conv_max_imgs = 0;
-  if (m->allow_tc)
-    for (const Step& st : p.steps)
-      if (conv_tc_candidate(st)) {
-        img_col = std::max(img_col, (size_t)(st.Ho * st.Wo) * (size_t)tc_padded_k(st.K) * sizeof(float));
-        img_out = std::max(img_out, (size_t)(st.Ho * st.Wo) * (size_t)st.N * sizeof(float));
-        conv_max_imgs = std::max<int64_t>(conv_max_imgs, st.static_rows ? st.rows_per_sample : p.max_batch);
-      }
-  int64_t conv_imgs = 0;
-  if (img_col) {
-    conv_imgs = (int64_t)std::max<size_t>(1, kConvWorkspaceBytes / (img_col + img_out));
-    conv_imgs = std::min<int64_t>(std::min<int64_t>(conv_imgs, conv_max_imgs), 65535);
-  }
-  const size_t col_b = round256((size_t)conv_imgs * img_col);
-  const size_t cout_b = round256((size_t)conv_imgs * img_out);
   // split-K partial sums: it runs only when at most half the SM pairs have a
   // whole 256-row tile, so at most 74 x 256 x 256 floats
   bool any_tc = false;
@@ -445,8 +422,8 @@ static int layout_block(Model* m, ExecCtx* c, size_t min_bytes, bool* did_alloc)
       if ((st.kind == ST_GEMM && tc_gemm_supported(st.K, st.N)) || conv_tc_candidate(st)) any_tc = true;
   const size_t ks_floats = any_tc ? kKsplitWorkspaceFloats : 0;
   const size_t ks_b = round256(ks_floats * sizeof(float));
-  const size_t bar_b = 256;  // chain-kernel barrier counters
-  const size_t need = std::max(arena + in_b + out_b + part_b + tick_b + col_b + cout_b + ks_b + bar_b, min_bytes);
+  const size_t bar_b = 1024;  // chain-kernel barrier counters at 0, two-layer team counters at 256
+  const size_t need = std::max(arena + in_b + out_b + part_b + tick_b + ks_b + bar_b, min_bytes);
   bool fresh = false;
   if (!c->block || c->block_bytes < need) {
     int rc = alloc_block(c, need);
@@ -461,16 +438,11 @@ static int layout_block(Model* m, ExecCtx* c, size_t min_bytes, bool* did_alloc)
   c->d_out = reinterpret_cast<float*>(c->block + arena + in_b);
   c->ws_part = max_n ? reinterpret_cast<float*>(c->block + arena + in_b + out_b) : nullptr;
   c->ws_tickets = max_n ? reinterpret_cast<unsigned*>(c->block + arena + in_b + out_b + part_b) : nullptr;
-  c->conv_imgs = conv_imgs;
-  c->ws_col = conv_imgs ? reinterpret_cast<float*>(c->block + arena + in_b + out_b + part_b + tick_b) : nullptr;
-  c->ws_cout = conv_imgs ? reinterpret_cast<float*>(c->block + arena + in_b + out_b + part_b + tick_b + col_b)
-                         : nullptr;
   c->ws_ksplit_floats = ks_floats;
-  c->ws_ksplit = ks_floats ? reinterpret_cast<float*>(c->block + arena + in_b + out_b + part_b + tick_b + col_b +
-                                                      cout_b)
-                           : nullptr;
-  c->chain_bar = reinterpret_cast<unsigned long long*>(c->block + arena + in_b + out_b + part_b + tick_b + col_b +
-                                                        cout_b + ks_b);
+  c->ws_ksplit = ks_floats ? reinterpret_cast<float*>(c->block + arena + in_b + out_b + part_b + tick_b) : nullptr;
+  c->chain_bar = reinterpret_cast<unsigned long long*>(c->block + arena + in_b + out_b + part_b + tick_b + ks_b);
+  c->team_flags = reinterpret_cast<unsigned*>(reinterpret_cast<char*>(c->chain_bar) + 256);
+  static_assert(256 + kTcMlpTeamFlagWords * sizeof(unsigned) <= 1024, "team counters fit the counter area");
   if (fresh && c->ws_tickets) {
     // tickets start at zero; every split-K launch leaves them at zero
     if (cudaMemset(c->ws_tickets, 0, tick_b) != cudaSuccess) {
@@ -594,46 +566,6 @@ static void copy_floats(const float* a, float* y, int64_t n, int sm, cudaStream_
 // Enqueues the launch list for `batch` rows on stream s.  With `marks`
 // (steps + 1 events) an event is recorded before every step and after the
 // last one, so per-step device times can be read back afterwards.
-// Convolution step on the tensor cores, in chunks of c->conv_imgs images:
-// im2col rows -> 3xTF32 GEMM (bias / ReLU epilogue per output channel) ->
-// NCHW.  Returns 0 when launched, 1 when the GEMM declines the shape (the
-// caller runs the SIMT convolution), -1 on a launch error.
-static int run_tc_conv(const Model* m, const Replica* rep, ExecCtx* c, const Step& st, const GemmArgs& a,
-                       const TcWeights& tw, int64_t imgs, int sm, cudaStream_t s) {
-  const int HoWo = (int)(st.Ho * st.Wo);
-  const int Kp = (int)st.Kp;
-  const int64_t in_img = st.Cin * st.H * st.W, out_img = st.N * (int64_t)HoWo;
-  for (int64_t b0 = 0; b0 < imgs; b0 += c->conv_imgs) {
-    const int64_t nb = std::min<int64_t>(c->conv_imgs, imgs - b0);
-    if (launch_im2col(a.A + b0 * in_img, c->ws_col, a.conv, (int)st.K, Kp, nb * HoWo, sm, s)) return -1;
-    TcArgs t{};
-    t.A = c->ws_col;
-    t.w_hi = tw.hi;
-    t.w_lo = tw.lo;
-    t.bias = a.bias;
-    t.res = nullptr;
-    t.Y = c->ws_cout;
-    t.M = nb * HoWo;
-    t.N = st.N;
-    t.K = Kp;
-    t.Kp = Kp;
-    t.epi = st.epi;
-    t.stall_test = m->tc_stall_test.load();
-    t.ws = c->ws_ksplit;
-    t.ws_floats = c->ws_ksplit_floats;
-    TcConfig cfg;
-    cfg.bn = st.tc_bn;
-    cfg.bk = st.tc_bk;
-    cfg.mh = st.tc_mh;
-    cfg.pair = st.tc_pair;
-    const int rc = launch_tc_gemm(t, tw, rep->err_dev, sm, s, cfg);
-    if (rc == 1 && b0 == 0) return 1;
-    if (rc != 0) return -1;
-    if (launch_rows_to_nchw(c->ws_cout, a.Y + b0 * out_img, nb, HoWo, (int)st.N, s)) return -1;
-  }
-  return 0;
-}
-
 static int enqueue(const Model* m, const Replica* rep, ExecCtx* c, const float* in, float* out, int64_t batch,
                    cudaStream_t s, cudaEvent_t* marks = nullptr) {
   char* arena = c->arena;
@@ -715,11 +647,33 @@ static int enqueue(const Model* m, const Replica* rep, ExecCtx* c, const float* 
           a.conv = rep->conv[i];
           const TcWeights& tw = rep->tc[i];
           int tc_rc = 1;  // 1: not taken
-          // convolutions of 32 output channels too: their im2col GEMMs have
-          // many rows, and the SIMT convolution is what they replace
-          if (!exact && tw.maps_ready && c->ws_col &&
+          // convolutions of 32 output channels too: their implicit GEMMs
+          // have many rows, and the SIMT convolution is what they replace
+          if (!exact && tw.maps_ready && M <= 0x7fffffff &&
               (policy == KP_TCGEN05 || (policy == KP_AUTO && M >= 128 && st.N >= 32 && st.Kp >= 32))) {
-            tc_rc = run_tc_conv(m, rep, c, st, a, tw, st.static_rows ? st.rows_per_sample : batch, sm, s);
+            TcConvParams cp;
+            std::memset(&cp, 0, sizeof(cp));
+            cp.x = a.A;
+            cp.ktab = a.conv.ktab;
+            cp.bias = a.bias;
+            cp.res = a.res;
+            cp.y = a.Y;
+            cp.M = (int)M;
+            cp.N = (int)st.N;
+            cp.K = (int)st.K;
+            cp.Cin = (int)st.Cin;
+            cp.H = (int)st.H;
+            cp.W = (int)st.W;
+            cp.Ho = (int)st.Ho;
+            cp.Wo = (int)st.Wo;
+            cp.sh = (int)st.conv.sh;
+            cp.sw = (int)st.conv.sw;
+            cp.ph = (int)st.conv.ph;
+            cp.pw = (int)st.conv.pw;
+            cp.epi = st.epi;
+            cp.err = rep->err_dev;
+            cp.stall_test = m->tc_stall_test.load();
+            tc_rc = launch_tc_conv(cp, tw, sm, s);
             if (tc_rc < 0) {
               set_error(std::string("tensor-core convolution launch failed: ") +
                         cudaGetErrorString(take_launch_error()));
@@ -727,7 +681,7 @@ static int enqueue(const Model* m, const Replica* rep, ExecCtx* c, const float* 
             }
           }
           if (tc_rc == 0) {
-            // im2col + tensor-core GEMM + NCHW
+            // implicit GEMM on the tensor cores, NCHW stores from the epilogue
           } else if (exact) {
             dispatch_simt<true, true>(a, sm, s);
           } else {
@@ -770,7 +724,10 @@ static int enqueue(const Model* m, const Replica* rep, ExecCtx* c, const float* 
             const TcWeights& tw2 = rep->tc[(size_t)st.mlp_step];
             auto plain = [](const Step& x) { return x.tc_bn == 0 && x.tc_bk == 0 && x.tc_mh == 0 && x.tc_pair == 0; };
             const TuneRecord* tr2 = s2.tuned_for(batch);
-            const bool asked = (tr ? tr->pair : st.tc_pair) == 4;
+            const int asked_pair = tr ? tr->pair : st.tc_pair;
+            const bool asked = asked_pair == 4 || asked_pair == 5;
+            // few tiles: layer 1 split over teams of pairs (by shape, or pair 5)
+            const bool team_ok = asked_pair == 5 || !asked;
             const bool by_shape = !tr && !tr2 && plain(st) && plain(s2) && tc_gemm_profitable(M, st.K, st.N) &&
                                   tc_gemm_profitable(M, s2.K, s2.N);
             if (asked || by_shape) {
@@ -783,6 +740,8 @@ static int enqueue(const Model* m, const Replica* rep, ExecCtx* c, const float* 
               t1.Kp = tw.Kp;
               t1.epi = st.epi;
               t1.stall_test = m->tc_stall_test.load();
+              t1.ws = c->ws_ksplit;
+              t1.ws_floats = c->ws_ksplit_floats;
               t2.A = nullptr;
               t2.bias = s2.bias.space ? ptr(s2.bias) : nullptr;
               t2.Y = ptr(s2.out);
@@ -800,7 +759,7 @@ static int enqueue(const Model* m, const Replica* rep, ExecCtx* c, const float* 
                 t2.head.n = (int)hs.N;
                 t2.head.epi = hs.epi;
               }
-              const int mrc = launch_tc_mlp(t1, tw, t2, tw2, rep->err_dev, s);
+              const int mrc = launch_tc_mlp(t1, tw, t2, tw2, rep->err_dev, s, team_ok ? c->team_flags : nullptr);
               if (mrc < 0) {
                 set_error(std::string("two-layer tensor-core launch failed: ") +
                           cudaGetErrorString(take_launch_error()));
@@ -838,7 +797,7 @@ static int enqueue(const Model* m, const Replica* rep, ExecCtx* c, const float* 
             cfg.bk = tr ? tr->bk : st.tc_bk;
             cfg.mh = tr ? tr->mh : st.tc_mh;
             cfg.pair = tr ? tr->pair : st.tc_pair;
-            if (cfg.pair == 4) cfg.pair = 0;  // the two-layer kernel did not apply: by shape
+            if (cfg.pair >= 4) cfg.pair = 0;  // the two-layer kernel did not apply: by shape
             const bool fuse_head = tr ? tr->fuse_head : st.fuse_head;
             if (st.head_step >= 0 && fuse_head) {
               const Step& hs = rep->steps[(size_t)st.head_step];
@@ -1279,8 +1238,8 @@ FTB_API int ftb_model_set_step_config(void* handle, int step, int tc_bn, int tc_
     return ST_CONFIG;
   }
   if (!(tc_bn == 0 || tc_bn == 64 || tc_bn == 128 || tc_bn == 256) || !(tc_bk == 0 || tc_bk == 16 || tc_bk == 32) ||
-      !(tc_mh >= 0 && tc_mh <= 2) || !(tc_pair >= 0 && tc_pair <= 4)) {
-    set_error("tile width must be 0, 64, 128 or 256, k-block 0, 16 or 32, row halves 0, 1 or 2, pair 0..4");
+      !(tc_mh >= 0 && tc_mh <= 2) || !(tc_pair >= 0 && tc_pair <= 5)) {
+    set_error("tile width must be 0, 64, 128 or 256, k-block 0, 16 or 32, row halves 0, 1 or 2, pair 0..5");
     return ST_CONFIG;
   }
   if (tc_pair >= 2 && tc_pair <= 3 && (tc_mh == 2 || (tc_bn != 0 && tc_bn < 128))) {

@@ -1,0 +1,312 @@
+// Convolution as an implicit GEMM on the tensor cores: no column matrix, no
+// layout pass.
+//
+//   y[b, co, oh, ow] = epi( sum_k col(m, k) W[co, k] ),   m = (b Ho + oh) Wo + ow
+//   col(m, k) = x[b, ci, oh sh - ph + kh dh, ow sw - pw + kw dw]   (0 outside the image)
+//   k = (ci Kh + kh) Kw + kw   (the reference's loop order, src/codegen.cpp:412-624)
+//
+// with the 3xTF32 arithmetic of tc_gemm.cuh (W^T = OIHW as [Cout, Kp], split
+// into tf32 hi / lo on the host; col split on the fly; fp32 accumulation in
+// TMEM).  Persistent, one CTA per SM over 128-pixel x BN-channel tiles, the
+// roles of tc_gemm.cuh with the A operand gathered instead of loaded by TMA:
+//   warp 0     TMA producer of the W^T k-blocks (16 k, hi and lo, 64-byte
+//              swizzle) into a STAGES-deep ring;
+//   warp 1     TMEM (two accumulators of BN columns) and the MMAs (one
+//              elected lane, tcgen05.mma kind::tf32 M=128 N=BN K=8, three
+//              per k-step);
+//   warps 2-5  the gather: thread t owns pixel m0 + t of the tile and, per
+//              k-block, reads its 16 input values (zero padding decided per
+//              value from a k-table of {ci H W + kh dh W + kw dw, kh dh,
+//              kw dw}), splits them into tf32 hi and lo and writes both rows
+//              in the layout TMA's 64-byte swizzle produces (16-byte chunk c
+//              of row r at chunk position c ^ ((r >> 1) & 3)); the next
+//              k-block's values are loaded while this one is written;
+//   warps 6-9  epilogue, overlapping the next tile's MMAs: tcgen05.ld (lane =
+//              pixel, 32 channels), bias / ReLU / residual in registers, and
+//              stores straight to NCHW (for one channel the 32 pixels of a
+//              warp are consecutive addresses of one plane).
+// Every mbarrier wait is bounded as in tc_gemm.cuh.
+#pragma once
+
+#include "tc_gemm.cuh"
+
+namespace ftb {
+
+struct TcConvParams {
+  const float* x;    // NCHW input
+  const int4* ktab;  // [K] gather table
+  const float* bias;  // [Cout] or null
+  const float* res;   // NCHW residual (same shape as y) or null
+  float* y;           // NCHW output
+  int M, N, K;        // pixels B*Ho*Wo, Cout, Cin*Kh*Kw
+  int Cin, H, W, Ho, Wo, sh, sw, ph, pw;
+  uint32_t epi;       // EPI_* (bias added after the k sum)
+  int* err;
+  int stall_test;
+};
+
+template <int BN, int STAGES>
+struct TcConvSmem {
+  static constexpr int A_BYTES = kTcBM * 16 * 4;  // one 16-k block of 128 pixels
+  static constexpr int B_BYTES = BN * 16 * 4;
+  static constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
+  static constexpr int TX_BYTES = 2 * B_BYTES;  // what TMA writes per stage
+  static constexpr int NBAR = 3 * STAGES + 6;
+  static constexpr int BAR_BYTES = 8 * NBAR + 16;
+  static constexpr int TOTAL = 1024 + STAGES * STAGE_BYTES + BAR_BYTES;
+};
+
+// The 16 values of col(m, kb*16 .. kb*16+15) for this thread's pixel.
+__device__ __forceinline__ void conv_gather16(float (&v)[16], const TcConvParams& p, const float* xb, int ih0,
+                                              int iw0, bool live, int kb) {
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const int k = kb * 16 + j;
+    float val = 0.0f;
+    if (live && k < p.K) {
+      const int4 e = __ldg(p.ktab + k);  // the same entry in every lane: a broadcast
+      const int ih = ih0 + e.y, iw = iw0 + e.z;
+      if (ih >= 0 && ih < p.H && iw >= 0 && iw < p.W) val = __ldg(xb + (ptrdiff_t)ih0 * p.W + iw0 + e.x);
+    }
+    v[j] = val;
+  }
+}
+
+// Row r (64 bytes) of a 64-byte-swizzled k-block tile: chunk c at c ^ ((r >> 1) & 3).
+__device__ __forceinline__ void conv_store_row(uint8_t* tile, int r, const float (&h)[16]) {
+  const int sw = (r >> 1) & 3;
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    float4* d = reinterpret_cast<float4*>(tile + r * 64 + ((c ^ sw) << 4));
+    *d = make_float4(h[4 * c], h[4 * c + 1], h[4 * c + 2], h[4 * c + 3]);
+  }
+}
+
+template <int BN, int STAGES>
+__global__ void __launch_bounds__(kTcThreads, 1)
+    tc_conv_kernel(const __grid_constant__ CUtensorMap map_bhi, const __grid_constant__ CUtensorMap map_blo,
+                   TcConvParams p) {
+  using L = TcConvSmem<BN, STAGES>;
+  static_assert(L::TOTAL <= 227 * 1024, "shared memory budget");
+  constexpr uint32_t TMEM_COLS = 2 * BN;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  auto a_tile = [&](int s) { return smem + s * L::STAGE_BYTES; };
+  auto alo_tile = [&](int s) { return smem + s * L::STAGE_BYTES + L::A_BYTES; };
+  auto bhi_tile = [&](int s) { return smem + s * L::STAGE_BYTES + 2 * L::A_BYTES; };
+  auto blo_tile = [&](int s) { return smem + s * L::STAGE_BYTES + 2 * L::A_BYTES + L::B_BYTES; };
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * L::STAGE_BYTES);
+  uint64_t* full = bars;                // W k-block landed
+  uint64_t* conv = bars + STAGES;       // A gathered and split (4 arrivals)
+  uint64_t* empty = bars + 2 * STAGES;  // MMAs done reading the stage
+  uint64_t* accf = bars + 3 * STAGES;   // [2] accumulator complete
+  uint64_t* acce = accf + 2;            // [2] accumulator drained (4 arrivals)
+  uint64_t* drain = acce + 2;           // MMAs retired after an abort
+  uint64_t* never = drain + 1;          // never arrived on (stall_test)
+  volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(never + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(never + 1) + 1;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int tiles_m = (p.M + kTcBM - 1) / kTcBM;
+  const int tiles_n = (p.N + BN - 1) / BN;
+  const int ntiles = tiles_m * tiles_n;
+  const int nk = (p.K + 15) / 16;
+  const int HoWo = p.Ho * p.Wo;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&conv[s], 4);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&accf[b], 1);
+      mbar_init(&acce[b], 4);
+    }
+    mbar_init(drain, 1);
+    mbar_init(never, 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(const_cast<uint32_t*>(tmem_slot))),
+                 "r"(TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  grid_dep_wait();
+  grid_dep_trigger();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    const uint64_t pol_w = l2_evict_last();  // every tile re-reads the weights
+    uint32_t it = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+      const int n0 = (t % tiles_n) * BN;
+      for (int kb = 0; kb < nk; ++kb, ++it) {
+        const int s = (int)(it % STAGES);
+        if (!(ok = mbar_wait_warp(&empty[s], ((it / STAGES) & 1u) ^ 1u, abort_flag, p.err, 1))) break;
+        if (elect_one()) {
+          mbar_arrive_expect_tx(&full[s], L::TX_BYTES);
+          tma_load_2d_hint(bhi_tile(s), &map_bhi, kb * 16, n0, &full[s], pol_w);
+          tma_load_2d_hint(blo_tile(s), &map_blo, kb * 16, n0, &full[s], pol_w);
+        }
+        __syncwarp();
+      }
+    }
+  } else if (warp == 1) {
+    const uint32_t idesc = idesc_tf32<BN>();
+    uint32_t it = 0, tc = 0;
+    bool ok = true;
+    if (p.stall_test) ok = mbar_wait_warp(never, 0, abort_flag, p.err, 9);
+    for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x, ++tc) {
+      const uint32_t buf = tc & 1u, use = tc >> 1;
+      if (!(ok = mbar_wait_warp(&acce[buf], (use & 1u) ^ 1u, abort_flag, p.err, 2))) break;
+      tc_fence_after();
+      const uint32_t d = tmem + buf * (uint32_t)BN;
+      for (int kb = 0; kb < nk; ++kb, ++it) {
+        const int s = (int)(it % STAGES);
+        if (!(ok = mbar_wait_warp(&conv[s], (it / STAGES) & 1u, abort_flag, p.err, 4))) break;
+        tc_fence_after();
+        const uint32_t ahi = smem_u32(a_tile(s)), alo = smem_u32(alo_tile(s));
+        const uint32_t bhi = smem_u32(bhi_tile(s)), blo = smem_u32(blo_tile(s));
+        if (elect_one()) {
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {  // K = 8 tf32 (32 bytes) per MMA
+            const uint32_t off = (uint32_t)j * 32u;
+            const uint64_t dbh = smem_desc_sw<16>(bhi + off), dbl = smem_desc_sw<16>(blo + off);
+            const uint64_t dah = smem_desc_sw<16>(ahi + off), dal = smem_desc_sw<16>(alo + off);
+            umma_tf32(d, dah, dbh, idesc, (kb > 0 || j > 0) ? 1u : 0u);
+            umma_tf32(d, dah, dbl, idesc, 1u);
+            umma_tf32(d, dal, dbh, idesc, 1u);
+          }
+          umma_commit(&empty[s]);
+        }
+        __syncwarp();
+      }
+      if (ok) {
+        if (elect_one()) umma_commit(&accf[buf]);
+        __syncwarp();
+      }
+    }
+    if (!ok) {
+      if (elect_one()) umma_commit(drain);
+      __syncwarp();
+      mbar_wait_warp(drain, 0, abort_flag, p.err, 5, /*ignore_abort=*/true);
+    }
+  } else if (warp < 6) {
+    // warps 2..5: gather, split, store; the next k-block's loads in flight
+    const int r = threadIdx.x - 64;  // this thread's pixel row of the tile
+    uint32_t it = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+      const int m = (t / tiles_n) * kTcBM + r;
+      const bool live = m < p.M;
+      const int b = live ? m / HoWo : 0;
+      const int pp = live ? m - b * HoWo : 0;
+      const int oh = pp / p.Wo, ow = pp - oh * p.Wo;
+      const int ih0 = oh * p.sh - p.ph, iw0 = ow * p.sw - p.pw;
+      const float* xb = p.x + (size_t)b * p.Cin * p.H * p.W;
+      float cur[16], nxt[16];
+      conv_gather16(cur, p, xb, ih0, iw0, live, 0);
+      for (int kb = 0; kb < nk; ++kb, ++it) {
+        if (kb + 1 < nk) conv_gather16(nxt, p, xb, ih0, iw0, live, kb + 1);
+        float h[16], l[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          h[j] = tf32_rna(cur[j]);
+          l[j] = tf32_rna(cur[j] - h[j]);
+        }
+        const int s = (int)(it % STAGES);
+        if (!(ok = mbar_wait_warp(&full[s], (it / STAGES) & 1u, abort_flag, p.err, 6))) break;
+        conv_store_row(a_tile(s), r, h);
+        conv_store_row(alo_tile(s), r, l);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&conv[s]);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) cur[j] = nxt[j];
+      }
+    }
+  } else {
+    // warps 6..9: epilogue, one TMEM lane quarter (32 pixels) each
+    const int q = warp & 3;
+    const uint32_t lanes = (uint32_t)(q * 32) << 16;
+    const bool bias = p.bias != nullptr && (p.epi & EPI_BIAS_LAST);
+    uint32_t tc = 0;
+    for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++tc) {
+      const uint32_t buf = tc & 1u, use = tc >> 1;
+      if (!mbar_wait_warp(&accf[buf], use & 1u, abort_flag, p.err, 7)) break;
+      tc_fence_after();
+      const int n0 = (t % tiles_n) * BN;
+      const int m = (t / tiles_n) * kTcBM + q * 32 + lane;
+      const bool live = m < p.M;
+      const int b = live ? m / HoWo : 0;
+      const int pp = live ? m - b * HoWo : 0;
+      const size_t base = (size_t)b * p.N * HoWo + pp;  // y[b, 0, pp]
+#pragma unroll 1
+      for (int c = 0; c < BN / 32 && n0 + 32 * c < p.N; ++c) {
+        uint32_t rr[32];
+        __syncwarp();
+        FTB_TMEM_LD32(tmem + buf * (uint32_t)BN + (uint32_t)(32 * c) + lanes, rr);
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        if (live) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int co = n0 + 32 * c + i;
+            if (co < p.N) {
+              float v = __uint_as_float(rr[i]);
+              if (bias) v = __fadd_rn(v, __ldg(p.bias + co));
+              if (p.epi & EPI_RELU_PRE) v = relu_keep_nan(v);
+              if (p.epi & EPI_RESIDUAL) v = __fadd_rn(v, p.res[base + (size_t)co * HoWo]);
+              if (p.epi & EPI_RELU_POST) v = relu_keep_nan(v);
+              p.y[base + (size_t)co * HoWo] = v;
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acce[buf]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+  }
+}
+
+template <int BN, int STAGES>
+inline int launch_tc_conv_bn(TcConvParams p, const TcWeights& w, int sm_count, cudaStream_t s) {
+  using L = TcConvSmem<BN, STAGES>;
+  static std::atomic<uint64_t> attr{0};
+  cudaError_t e = smem_limit_once(tc_conv_kernel<BN, STAGES>, L::TOTAL, attr);
+  if (e != cudaSuccess) return note_launch(e);
+  const int64_t ntiles = ((int64_t)(p.M + kTcBM - 1) / kTcBM) * ((p.N + BN - 1) / BN);
+  const unsigned grid = (unsigned)std::min<int64_t>(ntiles, sm_count);
+  const int bi = tc_bn_index(BN);
+  return note_launch(pdl_launch(tc_conv_kernel<BN, STAGES>, dim3(grid), dim3(kTcThreads), L::TOTAL, s,
+                                w.map_hi[1][bi], w.map_lo[1][bi], p));
+}
+
+// Returns 0 when launched, 1 when the shape does not fit (no weight maps,
+// too many pixels for 32-bit indices), -1 on a launch error.
+inline int launch_tc_conv(TcConvParams p, const TcWeights& w, int sm_count, cudaStream_t s) {
+  if (!w.maps_ready || p.M <= 0 || p.N <= 0 || p.K <= 0) return 1;
+  // the accumulator starts at zero: a bias-first epilogue adds the bias at the end
+  if (p.epi & EPI_BIAS_FIRST) p.epi = (p.epi & ~(uint32_t)EPI_BIAS_FIRST) | EPI_BIAS_LAST;
+  if (p.N <= 64) return launch_tc_conv_bn<64, 8>(p, w, sm_count, s);
+  if (p.N <= 128) return launch_tc_conv_bn<128, 6>(p, w, sm_count, s);
+  return launch_tc_conv_bn<256, 4>(p, w, sm_count, s);
+}
+
+}  // namespace ftb

@@ -23,6 +23,18 @@
 // The h tile (256 x N1 fp32) is never stored or re-read, and the two layers
 // share one launch.
 //
+// Few tiles (a tile count that leaves most pairs idle): a team of S pairs
+// (2 <= S <= 4) computes one tile.  Member s runs layer 1 over its own
+// contiguous range of k-blocks only; the helpers (s > 0) write their raw
+// layer-1 sums (this CTA's 128 rows x 256 columns) to a workspace and bump
+// the tile's per-CTA counter; the owner (s = 0) waits for S - 1 arrivals
+// (bounded), adds the helpers' sums to its own in member order while
+// converting h, and alone runs layer 2 and the head.  The k terms are then
+// associated differently from the unsplit kernel (deterministic, not the
+// same bits).  Every CTA counts itself out at the end; the last one resets
+// the counters, so each launch starts from zero, also after a wait that gave
+// up.
+//
 // Hazards on TMEM: layer 1 of the next tile overwrites columns [0, 256)
 // after layer 2 of this tile read its hi values there -- the MMAs of one
 // thread run in issue order, and the MMA warp issues that layer 1 only after
@@ -96,6 +108,25 @@ __device__ __forceinline__ void mlp_split_chunk(const uint32_t (&r)[32], const f
   }
 }
 
+// Adds the team helpers' raw sums of one chunk (32 floats of a row, at
+// src + j * stride for helper j + 1) to r, in member order.
+__device__ __forceinline__ void mlp_merge_chunk(uint32_t (&r)[32], const float* src, size_t stride, int helpers) {
+#pragma unroll 1
+  for (int j = 0; j < helpers; ++j) {
+    const float4* s4 = reinterpret_cast<const float4*>(src + (size_t)j * stride);
+    float4 v4[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v4[i] = __ldcg(s4 + i);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      r[4 * i + 0] = __float_as_uint(__fadd_rn(__uint_as_float(r[4 * i + 0]), v4[i].x));
+      r[4 * i + 1] = __float_as_uint(__fadd_rn(__uint_as_float(r[4 * i + 1]), v4[i].y));
+      r[4 * i + 2] = __float_as_uint(__fadd_rn(__uint_as_float(r[4 * i + 2]), v4[i].z));
+      r[4 * i + 3] = __float_as_uint(__fadd_rn(__uint_as_float(r[4 * i + 3]), v4[i].w));
+    }
+  }
+}
+
 constexpr int kTcMlpN1 = 256;  // layer 1's width: its accumulator is TMEM columns [0, 256)
 constexpr int kTcMlpN2 = 128;  // layer 2's width: columns [256, 384)
 
@@ -113,6 +144,18 @@ struct TcMlpSmem {
   static constexpr int TOTAL = 1024 + STAGES * STAGE_BYTES + EPI_BYTES + HEAD_BYTES + BAR_BYTES;
 };
 
+// Split of layer 1 over a team of pairs (S = 1: no split).
+struct TcMlpTeam {
+  float* ws;         // helper sums: [((tile (S-1) + s-1) 2 + rank) 128 + row] x 256 floats
+  unsigned* flags;   // [2 tiles]: helper CTAs that published their sums, per tile and CTA rank
+  unsigned* depart;  // CTAs that left the launch
+  int S;
+  int pad;
+};
+
+constexpr int kTcMlpMaxTeam = 4;
+constexpr int kTcMlpTeamFlagWords = 160;  // 2 x tiles (<= 74) + the departure counter, rounded
+
 // p1: layer 1 (M, K = K1, N = N1, bias, epi); p2: layer 2 (K = N1, N = N2,
 // bias, epi, output Y / head).  Roles as in the SM-pair kernel; the
 // epilogue warps also convert h.
@@ -121,7 +164,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
     tc_mlp_pair_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_w1hi,
                        const __grid_constant__ CUtensorMap map_w1lo, const __grid_constant__ CUtensorMap map_w2hi,
                        const __grid_constant__ CUtensorMap map_w2lo, const __grid_constant__ CUtensorMap map_y,
-                       TcKernelParams p1, TcKernelParams p2) {
+                       TcKernelParams p1, TcKernelParams p2, TcMlpTeam team) {
   using L = TcMlpSmem<STAGES>;
   static_assert(L::TOTAL <= 227 * 1024, "shared memory budget");
   constexpr uint32_t TMEM_COLS = 512, ACC2 = 256, LO = 384;
@@ -146,6 +189,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
   uint64_t* never = drain + 1;          // never arrived on (stall_test)
   volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(never + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(never + 1) + 1;
+  volatile int* team_ok = reinterpret_cast<volatile int*>(never + 1) + 2;  // owner: the helpers' sums arrived
 
   const uint32_t rank = cluster_ctarank();
   const uint32_t peer = rank ^ 1u;
@@ -157,6 +201,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
   const int nch = (p1.N + 31) / 32;  // chunks of h converted per tile
   const int pair = (int)cluster_index();
   const int npairs = (int)cluster_count();
+  // this pair's tiles and layer-1 k-blocks: all of them, or in a team one
+  // tile and the member's contiguous share of the k-blocks
+  const int S = team.S;
+  const bool teamed = S > 1;
+  const int u_first = teamed ? pair % tiles : pair;
+  const int member = teamed ? pair / tiles : 0;
+  const bool owner = member == 0;
+  const int kb_lo = teamed ? (member * nk1) / S : 0;
+  const int kb_hi = teamed ? ((member + 1) * nk1) / S : nk1;
+  const int nkl = kb_hi - kb_lo;
+  auto u_next = [&](int u) { return teamed ? tiles : u + npairs; };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -197,9 +252,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
     const uint64_t pol_w = l2_evict_last();   // both weights are re-read by every tile
     uint32_t it = 0;
     bool ok = true;
-    for (int u = pair; u < tiles && ok; u += npairs) {
+    for (int u = u_first; u < tiles && ok; u = u_next(u)) {
       const int m0 = u * 256 + (int)rank * kTcBM;
-      for (int kb = 0; kb < nk1; ++kb, ++it) {
+      for (int kb = kb_lo; kb < kb_hi; ++kb, ++it) {
         const int s = (int)(it % STAGES);
         if (!(ok = pair_wait_warp(&empty[s], ((it / STAGES) & 1u) ^ 1u, abort_flag, peer_abort, p1.err, 1))) break;
         if (elect_one()) {
@@ -210,7 +265,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
         }
         __syncwarp();
       }
-      for (int j = 0; j < nk2 && ok; ++j, ++it) {
+      for (int j = 0; j < nk2 && ok && owner; ++j, ++it) {
         const int s = (int)(it % STAGES);
         if (!(ok = pair_wait_warp(&empty[s], ((it / STAGES) & 1u) ^ 1u, abort_flag, peer_abort, p1.err, 1))) break;
         if (elect_one()) {
@@ -227,10 +282,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
       bool ok = true;
       if (p1.stall_test) ok = pair_wait_warp(never, 0, abort_flag, peer_abort, p1.err, 9);
       const uint32_t idesc1 = idesc_tf32_pair(256), idesc2 = idesc_tf32_pair(kTcMlpN2);
-      for (int u = pair; u < tiles && ok; u += npairs, ++tc) {
+      for (int u = u_first; u < tiles && ok; u = u_next(u), ++tc) {
         // layer 1 into columns [0, 256); this tile's layer 2 of the previous
         // tile, issued earlier, has read its A there first
-        for (int kb = 0; kb < nk1; ++kb, ++it) {
+        for (int kb = kb_lo; kb < kb_hi; ++kb, ++it) {
           const int s = (int)(it % STAGES);
           if (!(ok = pair_wait_warp(&conv[s], (it / STAGES) & 1u, abort_flag, peer_abort, p1.err, 4))) break;
           tc_fence_after();
@@ -243,7 +298,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
               const uint32_t off = (uint32_t)k8 * 32u;
               const uint64_t dbh = smem_desc_sw<16>(bhi + off), dbl = smem_desc_sw<16>(blo + off);
               const uint64_t dah = smem_desc_sw<16>(ahi + off), dal = smem_desc_sw<16>(alo + off);
-              umma2_tf32(tmem, dah, dbh, idesc1, (kb > 0 || k8 > 0) ? 1u : 0u);
+              umma2_tf32(tmem, dah, dbh, idesc1, (kb > kb_lo || k8 > 0) ? 1u : 0u);
               umma2_tf32(tmem, dah, dbl, idesc1, 1u);
               umma2_tf32(tmem, dal, dbh, idesc1, 1u);
             }
@@ -261,6 +316,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
           }
           __syncwarp();
         }
+        if (!owner) continue;  // a helper's part ends with its layer-1 sums
         // layer 2 into columns [256, 384), once the previous tile's epilogue drained them
         if (!(ok = pair_wait_warp(acce2, (tc & 1u) ^ 1u, abort_flag, peer_abort, p1.err, 2))) break;
         tc_fence_after();
@@ -322,11 +378,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
     const int t128 = threadIdx.x - 64;
     uint32_t it = 0;
     bool ok = true;
-    for (int u = pair; u < tiles && ok; u += npairs) {
-      for (int kb = 0; kb < nk1 + nk2; ++kb, ++it) {
+    for (int u = u_first; u < tiles && ok; u = u_next(u)) {
+      for (int kb = 0; kb < nkl + (owner ? nk2 : 0); ++kb, ++it) {
         const int s = (int)(it % STAGES);
         if (!(ok = pair_wait_warp(&full[s], (it / STAGES) & 1u, abort_flag, peer_abort, p1.err, 6))) break;
-        if (kb < nk1) {
+        if (kb < nkl) {
           tc_split_a<(kTcBM * 16 / 4) / 128>(reinterpret_cast<float4*>(a_tile(s)),
                                              reinterpret_cast<float4*>(alo_tile(s)), t128);
           fence_proxy_async_smem();
@@ -356,18 +412,74 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
     const bool ep_relu = (p1.epi & (EPI_RELU_PRE | EPI_RELU_POST)) != 0;
     uint32_t tc = 0, g = 0;
     bool ok = true;
-    for (int u = pair; u < tiles && ok; u += npairs, ++tc) {
+    for (int u = u_first; u < tiles && ok; u = u_next(u), ++tc) {
       const int m0 = u * 256 + (int)rank * kTcBM;
       if (!(ok = pair_wait_warp(accf1, tc & 1u, abort_flag, peer_abort, p1.err, 7))) break;
       tc_fence_after();
       // chunk c+1 is loaded from TMEM while chunk c's stores complete
       uint32_t r[32];
+      const int row = q * 32 + lane;  // this thread's row of the CTA's 128
+      if (!owner) {
+        // helper: publish this CTA's raw layer-1 sums, then count them in
+        float* dst = team.ws + ((size_t)((u * (S - 1) + member - 1) * 2 + (int)rank) * 128 + row) * 256;
+        for (int c = 0; c < nch; ++c) {
+          __syncwarp();
+          FTB_TMEM_LD32(tmem + lanes + (uint32_t)(32 * c), r);
+          FTB_TMEM_WAIT_LD32(r);
+          float4* d4 = reinterpret_cast<float4*>(dst + 32 * c);
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            d4[i] = make_float4(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1]),
+                                __uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3]));
+        }
+        tc_fence_before();
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (threadIdx.x == 192) {
+          __threadfence();
+          atomicAdd(team.flags + 2 * u + (int)rank, 1u);
+        }
+        continue;
+      }
+      if (teamed) {
+        // owner: the S - 1 helpers of this tile have published this CTA's rows
+        if (threadIdx.x == 192) {
+          int tok = 1;
+          const unsigned* f = team.flags + 2 * u + (int)rank;
+          const uint64_t t0 = global_ns();
+          for (uint32_t it2 = 0;; ++it2) {
+            unsigned v;
+            asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+            if ((int)v >= S - 1) break;
+            if ((it2 & 63u) == 63u) {
+              if (*abort_flag) {
+                tok = 0;
+                break;
+              }
+              if (global_ns() - t0 > kTcWaitLimitNs) {
+                *abort_flag = 1;
+                st_cluster_u32(peer_abort, 1u);
+                atomicCAS(p1.err, 0, 10);
+                tok = 0;
+                break;
+              }
+            }
+            __nanosleep(32);
+          }
+          *team_ok = tok;
+        }
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (!(ok = *team_ok != 0)) break;
+      }
+      // the helpers' sums of this thread's row, chunk c at 32 c
+      const float* hrow = team.ws + ((size_t)(u * (S - 1) * 2 + (int)rank) * 128 + row) * 256;
+      const size_t hstride = (size_t)2 * 128 * 256;  // from one member's sums to the next
       __syncwarp();
       FTB_TMEM_LD32(tmem + lanes, r);
       FTB_TMEM_WAIT_LD32(r);
       for (int c = 0; c < nch; ++c) {
         const uint32_t gc = g + (uint32_t)c, qs = gc & 3u, use = gc >> 2;
         uint32_t hi[32], lo[32];
+        if (teamed) mlp_merge_chunk(r, hrow + 32 * c, hstride, S - 1);
         const float* b = b1s + 32 * c;
         if (ep_bias && ep_relu) mlp_split_chunk<true, true>(r, b, hi, lo);
         else if (ep_bias) mlp_split_chunk<true, false>(r, b, hi, lo);
@@ -406,6 +518,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
     __syncwarp();
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+  }
+  if (teamed && threadIdx.x == 0) {
+    // every role of this CTA is done: count it out; the last CTA resets the counters
+    __threadfence();
+    const unsigned d = atomicAdd(team.depart, 1u);
+    if (d == gridDim.x - 1) {
+      for (int i = 0; i < 2 * tiles; ++i) atomicExch(team.flags + i, 0u);
+      atomicExch(team.depart, 0u);
+    }
   }
 }
 
@@ -449,10 +570,21 @@ inline bool tc_mlp_supported(const TcArgs& t1, const TcWeights& w1, const TcArgs
   return true;
 }
 
+// Team size for `tiles` tiles of layer 1 with nk1 k-blocks: split when at
+// least two pairs per tile are free, at most four, each member keeping at
+// least eight k-blocks.
+inline int tc_mlp_team_size(int64_t tiles, int nk1, int max_pairs) {
+  if (tiles <= 0) return 1;
+  int S = (int)std::min<int64_t>(kTcMlpMaxTeam, max_pairs / tiles);
+  S = std::min(S, nk1 / 8);
+  return S >= 2 ? S : 1;
+}
+
 // Returns 0 when launched, 1 when the pair of layers cannot take this path,
-// -1 on a launch error.
+// -1 on a launch error.  With `team_flags` (kTcMlpTeamFlagWords zeroed words)
+// and the split-K workspace in t1.ws, few tiles run split over teams of pairs.
 inline int launch_tc_mlp(const TcArgs& t1, const TcWeights& w1, const TcArgs& t2, const TcWeights& w2, int* err,
-                         cudaStream_t s) {
+                         cudaStream_t s, unsigned* team_flags = nullptr) {
   constexpr int STAGES = 6;
   using L = TcMlpSmem<STAGES>;
   if (!tc_mlp_supported(t1, w1, t2, w2)) return 1;
@@ -486,11 +618,26 @@ inline int launch_tc_mlp(const TcArgs& t1, const TcWeights& w1, const TcArgs& t2
   std::memset(&map_y, 0, sizeof(map_y));
   p2.y_tma = (t2.head.n == 0 && make_map_3d_out(&map_y, t2.Y, 1, t2.M, t2.N)) ? 1 : 0;
   const int64_t tiles = (t1.M + 255) / 256;
-  const unsigned pairs = (unsigned)std::min<int64_t>(tiles, max_pairs);
+  unsigned pairs = (unsigned)std::min<int64_t>(tiles, max_pairs);
+  TcMlpTeam team;
+  std::memset(&team, 0, sizeof(team));
+  team.S = 1;
+  if (team_flags && t1.ws) {
+    const int S = tc_mlp_team_size(tiles, (int)((t1.K + 15) / 16), max_pairs);
+    const size_t need = (size_t)(S - 1) * (size_t)tiles * 2 * 128 * 256;
+    if (S > 1 && need <= t1.ws_floats && 2 * tiles <= kTcMlpTeamFlagWords - 1) {
+      team.S = S;
+      team.ws = t1.ws;
+      team.flags = team_flags;
+      team.depart = team_flags + kTcMlpTeamFlagWords - 1;
+      pairs = (unsigned)(tiles * S);
+    }
+  }
   // W1^T halves of 128 rows, W2^T halves of 64 rows, k-blocks of 16
   return note_launch(pdl_launch(tc_mlp_pair_kernel<STAGES>, dim3(2 * pairs), dim3(kTcThreads), L::TOTAL, s, map_a,
                                 w1.map_hi[1][tc_bn_index(128)], w1.map_lo[1][tc_bn_index(128)],
-                                w2.map_hi[1][tc_bn_index(64)], w2.map_lo[1][tc_bn_index(64)], map_y, p1, p2));
+                                w2.map_hi[1][tc_bn_index(64)], w2.map_lo[1][tc_bn_index(64)], map_y, p1, p2,
+                                team));
 }
 
 }  // namespace ftb

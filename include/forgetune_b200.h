@@ -123,18 +123,21 @@ FORGETUNE_EXPORT int ftb_model_set_devices(void* model, const int* device_ids, i
 FORGETUNE_EXPORT int ftb_model_set_policy(void* model, int policy);
 /* Tensor-core tile of launch-list step `step`: width tc_bn (0, 64, 128, 256),
  * k-block tc_bk (0, 16, 32), rows tc_mh x 128 on one SM (0, 1, 2; 2 needs
- * tc_bn <= 128), tc_pair (0..4): 2 = 256-row tiles computed by an SM pair
+ * tc_bn <= 128), tc_pair (0..5): 2 = 256-row tiles computed by an SM pair
  * (tcgen05 cta_group::2; needs tc_bn 0, 128 or 256 and tc_mh 0 or 1), 3 = the
  * same with split-K when the tiles cannot occupy the pairs (k ranges summed
  * in a fixed order), 1 = one SM per tile, 4 = this step and the next GEMM in
  * one launch with this step's output kept in tensor memory (where the step
- * pair qualifies: `mlp_step` in ftb_describe_blob's output; else as 0);
- * 0 = chosen by shape (may pick split-K, or the two-layer launch when
- * neither step carries a configuration).  fuse_head: compute a following
- * small-N head in the epilogue.
- * For the autotuner; call between runs.  The choices other than split-K give
- * bit-identical results; split-K changes the order of the k sums (still
- * deterministic run to run). */
+ * pair qualifies: `mlp_step` in ftb_describe_blob's output; else as 0),
+ * 5 = the same, with this step's k-blocks split over a team of 2-4 pairs per
+ * tile when the tiles leave at least two pairs each free (the helpers' sums
+ * are added to the owner's in member order);
+ * 0 = chosen by shape (may pick split-K, or the two-layer launch, split over
+ * teams when the tiles are few, when neither step carries a configuration).
+ * fuse_head: compute a following small-N head in the epilogue.
+ * For the autotuner; call between runs.  The choices other than split-K and
+ * team splits give bit-identical results; those change the order of the k
+ * sums (still deterministic run to run). */
 FORGETUNE_EXPORT int ftb_model_set_step_config(void* model, int step, int tc_bn, int tc_bk, int tc_mh, int tc_pair,
                                                int fuse_head);
 /* Tuned kernel table (the autotuner's result): n records of 9 int64 each,

@@ -53,11 +53,13 @@ def test_tensor_core_wait_timeout_is_reported_and_recoverable(pair, tmp_path):
     cm.close()
 
 
-def test_two_layer_kernel_wait_timeout_is_reported_and_recoverable(tmp_path):
+@pytest.mark.parametrize("pair,rows", [(4, 3000), (5, 2048)])
+def test_two_layer_kernel_wait_timeout_is_reported_and_recoverable(pair, rows, tmp_path):
     """The two-layer kernel (both layers and the head in one launch, the
-    hidden layer in tensor memory): its MMA thread's wait runs out, every
-    role of both CTAs leaves through its own bounded waits, the run returns
-    -5, and the same context then computes correctly again."""
+    hidden layer in tensor memory), unsplit and split over teams of pairs:
+    its MMA thread's wait runs out, every role of both CTAs leaves through
+    its own bounded waits (a team owner also stops waiting for its helpers),
+    the run returns -5, and the same context then computes correctly again."""
     torch.manual_seed(4)
     m = nn.Sequential(nn.Linear(256, 256), nn.ReLU(), nn.Linear(256, 128), nn.ReLU(), nn.Linear(128, 10)).eval()
     cm = compile_model(m, (torch.randn(2, 256),), output_dir=str(tmp_path), autotune=False, enable_fusion=True,
@@ -67,9 +69,9 @@ def test_two_layer_kernel_wait_timeout_is_reported_and_recoverable(tmp_path):
         eng = _native.EngineModel(f.read())
     eng.set_devices([torch.cuda.current_device()])
     assert eng.describe()["steps"][0]["mlp_step"] == 1
-    eng.set_step_config(0, 0, 0, 0, 4, True)
-    x = np.random.default_rng(1).standard_normal((3000, 256)).astype(np.float32)
-    y = np.zeros((3000, 10), np.float32)
+    eng.set_step_config(0, 0, 0, 0, pair, True)  # pair 5 at 8 tiles: layer 1 split over teams of 2 pairs
+    x = np.random.default_rng(1).standard_normal((rows, 256)).astype(np.float32)
+    y = np.zeros((rows, 10), np.float32)
     assert eng.run(x, y) == 0
     want = oracle.run_model(m, x, "naive_ijk")
     assert np.allclose(y, want, atol=1e-4, rtol=1e-4)
@@ -81,6 +83,36 @@ def test_two_layer_kernel_wait_timeout_is_reported_and_recoverable(tmp_path):
     assert "exceeded its limit" in _native.last_error()
 
     assert lib.ftb_model_set_fault_injection(eng.handle, 0) == 0
+    assert eng.run(x, y) == 0, _native.last_error()
+    assert np.allclose(y, want, atol=1e-4, rtol=1e-4)
+    eng.close()
+    cm.close()
+
+
+def test_convolution_wait_timeout_is_reported_and_recoverable(tmp_path):
+    """The implicit-GEMM convolution's MMA thread waits on a barrier nothing
+    completes: the wait runs out, the gather, producer and epilogue warps
+    leave through their bounded waits, the run returns -5, and the same
+    context then computes correctly again."""
+    torch.manual_seed(6)
+    m = nn.Sequential(nn.Conv2d(8, 64, 3, padding=1), nn.ReLU()).eval()
+    cm = compile_model(m, (torch.randn(2, 8, 16, 16),), output_dir=str(tmp_path), autotune=False,
+                       enable_fusion=True, kernel_variant="fused_ikj", dynamic_batch=True, max_batch_size=64,
+                       gpu_kernel="tcgen05", verify=False)
+    with open(cm.manifest()["artifacts"]["graph_blob"], "rb") as f:
+        eng = _native.EngineModel(f.read())
+    eng.set_devices([torch.cuda.current_device()])
+    x = np.random.default_rng(2).standard_normal((16, 8, 16, 16)).astype(np.float32)
+    y = np.zeros((16, 64, 16, 16), np.float32)
+    want = oracle.run_model(m, x, "fused_ikj")
+    assert eng.run(x, y) == 0
+    assert np.allclose(y, want, atol=1e-4, rtol=1e-4)
+    lib = _native.lib()
+    assert lib.ftb_model_set_fault_injection(eng.handle, 1) == 0
+    assert eng.run(x, y) == -5
+    assert "exceeded its limit" in _native.last_error()
+    assert lib.ftb_model_set_fault_injection(eng.handle, 0) == 0
+    y[:] = 0
     assert eng.run(x, y) == 0, _native.last_error()
     assert np.allclose(y, want, atol=1e-4, rtol=1e-4)
     eng.close()

@@ -156,14 +156,17 @@ CONVS = [
     (64, 64, 8, 8, 64, 3, 2, 1, 1, False),
     (7, 5, 13, 11, 40, 3, 1, 2, 2, True),        # dilation 2, Cout not a multiple of 32, odd sizes
     (3, 8, 9, 9, 48, 1, 1, 0, 1, False),         # 1x1
-    (100, 16, 64, 64, 32, 3, 1, 1, 1, True),     # workspace chunks: ~80 images per chunk
+    (100, 16, 64, 64, 32, 3, 1, 1, 1, True),     # 409600 pixels: 3200 tiles over the SMs
+    (5, 12, 10, 10, 96, 3, 1, 1, 1, True),       # 128-channel tiles, 96 in range
+    (2, 4, 15, 17, 300, 5, 2, 2, 1, False),      # 256-channel tiles: two column tiles, the second partial
 ]
 
 
 @pytest.mark.parametrize("B,Cin,H,W,Cout,k,stride,pad,dil,relu", CONVS)
 def test_tcgen05_convolution_matches_oracle(B, Cin, H, W, Cout, k, stride, pad, dil, relu, tmp_path):
-    """Convolution as im2col rows + the 3xTF32 GEMM + NCHW, against the oracle's
-    direct convolution with the reference's tolerance, bitwise run to run."""
+    """Convolution as an implicit GEMM on the tensor cores (the input gathered
+    per k-block, NCHW stores from the epilogue), against the oracle's direct
+    convolution with the reference's tolerance, bitwise run to run."""
     torch.manual_seed(Cin * 100 + Cout)
     layers = [nn.Conv2d(Cin, Cout, k, stride=stride, padding=pad, dilation=dil)]
     if relu:
