@@ -15,9 +15,11 @@
 //              elected lane, tcgen05.mma kind::tf32 M=128 N=BN K=8, three
 //              per k-step);
 //   warps 2-5  the gather: thread t owns pixel m0 + t of the tile and, per
-//              k-block, reads its 16 input values (zero padding decided per
-//              value from a k-table of {ci H W + kh dh W + kw dw, kh dh,
-//              kw dw}), splits them into tf32 hi and lo and writes both rows
+//              k-block, issues its 16 input loads at once (zero padding
+//              decided per value from a k-table of {ci H W + kh dh W + kw dw,
+//              kh dh, kw dw} staged in shared memory; a value outside the
+//              image loads a valid address and is zeroed by a mask), splits
+//              them into tf32 hi and lo and writes both rows
 //              in the layout TMA's 64-byte swizzle produces (16-byte chunk c
 //              of row r at chunk position c ^ ((r >> 1) & 3)); the next
 //              k-block's values are loaded while this one is written;
@@ -53,23 +55,29 @@ struct TcConvSmem {
   static constexpr int TX_BYTES = 2 * B_BYTES;  // what TMA writes per stage
   static constexpr int NBAR = 3 * STAGES + 6;
   static constexpr int BAR_BYTES = 8 * NBAR + 16;
-  static constexpr int TOTAL = 1024 + STAGES * STAGE_BYTES + BAR_BYTES;
+  static constexpr int KTAB_MAX = 1024;  // k-table entries staged in shared memory (K <= 1024)
+  static constexpr int KTAB_BYTES = KTAB_MAX * 16;
+  static constexpr int TOTAL = 1024 + STAGES * STAGE_BYTES + BAR_BYTES + KTAB_BYTES;
 };
 
-// The 16 values of col(m, kb*16 .. kb*16+15) for this thread's pixel.
-__device__ __forceinline__ void conv_gather16(float (&v)[16], const TcConvParams& p, const float* xb, int ih0,
-                                              int iw0, bool live, int kb) {
+// Issues the 16 loads of col(m, kb*16 .. kb*16+15) for this thread's pixel
+// at once: the k-table comes from shared memory, a value outside the image
+// (or past K) loads the image's first element instead and is zeroed later by
+// its bit in *valid, so no load waits on another.
+__device__ __forceinline__ void conv_gather16(float (&v)[16], uint32_t* valid, const int4* ktab_s, int K, int H,
+                                              int W, const float* xb, int ih0, int iw0, bool live, int kb) {
+  uint32_t ok = 0;
 #pragma unroll
   for (int j = 0; j < 16; ++j) {
     const int k = kb * 16 + j;
-    float val = 0.0f;
-    if (live && k < p.K) {
-      const int4 e = __ldg(p.ktab + k);  // the same entry in every lane: a broadcast
-      const int ih = ih0 + e.y, iw = iw0 + e.z;
-      if (ih >= 0 && ih < p.H && iw >= 0 && iw < p.W) val = __ldg(xb + (ptrdiff_t)ih0 * p.W + iw0 + e.x);
-    }
-    v[j] = val;
+    const int4 e = ktab_s[k < K ? k : 0];
+    const int ih = ih0 + e.y, iw = iw0 + e.z;
+    const bool in = live && k < K && ih >= 0 && ih < H && iw >= 0 && iw < W;
+    const float* a = in ? xb + ((ptrdiff_t)ih0 * W + iw0 + e.x) : xb;
+    v[j] = __ldg(a);
+    ok |= (in ? 1u : 0u) << j;
   }
+  *valid = ok;
 }
 
 // Row r (64 bytes) of a 64-byte-swizzled k-block tile: chunk c at c ^ ((r >> 1) & 3).
@@ -105,6 +113,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   uint64_t* never = drain + 1;          // never arrived on (stall_test)
   volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(never + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(never + 1) + 1;
+  int4* ktab_s = reinterpret_cast<int4*>(smem + STAGES * L::STAGE_BYTES + L::BAR_BYTES);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -142,6 +151,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   grid_dep_wait();
   grid_dep_trigger();
   const uint32_t tmem = *tmem_slot;
+  // the gather warps stage the k-table (a weight-side constant, K <= KTAB_MAX)
+  if (warp >= 2 && warp < 6) {
+    for (int k = threadIdx.x - 64; k < p.K; k += 128) ktab_s[k] = __ldg(p.ktab + k);
+    asm volatile("bar.sync 2, 128;" ::: "memory");
+  }
 
   if (warp == 0) {
     const uint64_t pol_w = l2_evict_last();  // every tile re-reads the weights
@@ -214,14 +228,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       const int ih0 = oh * p.sh - p.ph, iw0 = ow * p.sw - p.pw;
       const float* xb = p.x + (size_t)b * p.Cin * p.H * p.W;
       float cur[16], nxt[16];
-      conv_gather16(cur, p, xb, ih0, iw0, live, 0);
+      uint32_t vcur = 0, vnxt = 0;
+      conv_gather16(cur, &vcur, ktab_s, p.K, p.H, p.W, xb, ih0, iw0, live, 0);
       for (int kb = 0; kb < nk; ++kb, ++it) {
-        if (kb + 1 < nk) conv_gather16(nxt, p, xb, ih0, iw0, live, kb + 1);
+        if (kb + 1 < nk) conv_gather16(nxt, &vnxt, ktab_s, p.K, p.H, p.W, xb, ih0, iw0, live, kb + 1);
         float h[16], l[16];
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
-          h[j] = tf32_rna(cur[j]);
-          l[j] = tf32_rna(cur[j] - h[j]);
+          const float c = (vcur >> j) & 1u ? cur[j] : 0.0f;
+          h[j] = tf32_rna(c);
+          l[j] = tf32_rna(c - h[j]);
         }
         const int s = (int)(it % STAGES);
         if (!(ok = mbar_wait_warp(&full[s], (it / STAGES) & 1u, abort_flag, p.err, 6))) break;
@@ -232,6 +248,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         if (lane == 0) mbar_arrive(&conv[s]);
 #pragma unroll
         for (int j = 0; j < 16; ++j) cur[j] = nxt[j];
+        vcur = vnxt;
       }
     }
   } else {
@@ -301,7 +318,7 @@ inline int launch_tc_conv_bn(TcConvParams p, const TcWeights& w, int sm_count, c
 // Returns 0 when launched, 1 when the shape does not fit (no weight maps,
 // too many pixels for 32-bit indices), -1 on a launch error.
 inline int launch_tc_conv(TcConvParams p, const TcWeights& w, int sm_count, cudaStream_t s) {
-  if (!w.maps_ready || p.M <= 0 || p.N <= 0 || p.K <= 0) return 1;
+  if (!w.maps_ready || p.M <= 0 || p.N <= 0 || p.K <= 0 || p.K > TcConvSmem<64, 8>::KTAB_MAX) return 1;
   // the accumulator starts at zero: a bias-first epilogue adds the bias at the end
   if (p.epi & EPI_BIAS_FIRST) p.epi = (p.epi & ~(uint32_t)EPI_BIAS_FIRST) | EPI_BIAS_LAST;
   if (p.N <= 64) return launch_tc_conv_bn<64, 8>(p, w, sm_count, s);

@@ -23,13 +23,15 @@
 // The h tile (256 x N1 fp32) is never stored or re-read, and the two layers
 // share one launch.
 //
-// Few tiles (a tile count that leaves most pairs idle): a team of S pairs
-// (2 <= S <= 4) computes one tile.  Member s runs layer 1 over its own
-// contiguous range of k-blocks only; the helpers (s > 0) write their raw
-// layer-1 sums (this CTA's 128 rows x 256 columns) to a workspace and bump
-// the tile's per-CTA counter; the owner (s = 0) waits for S - 1 arrivals
-// (bounded), adds the helpers' sums to its own in member order while
-// converting h, and alone runs layer 2 and the head.  The k terms are then
+// Few tiles (a tile count that leaves at least one idle pair per tile): a
+// team of S = 2 pairs computes one tile.  Member s runs layer 1 over its own
+// contiguous half of the k-blocks only; the helper (s = 1) writes its raw
+// layer-1 sums (this CTA's 128 rows x 256 columns) to a workspace and bumps
+// the tile's per-CTA counter; the owner (s = 0) waits for it (bounded), adds
+// the helper's sums to its own while converting h (each chunk's sums loaded
+// while the previous chunk is converted), and alone runs layer 2 and the
+// head.  (Teams of more pairs were slower: the owner's added L2 round trips
+// per chunk outweighed the shorter layer 1.)  The k terms are then
 // associated differently from the unsplit kernel (deterministic, not the
 // same bits).  Every CTA counts itself out at the end; the last one resets
 // the counters, so each launch starts from zero, also after a wait that gave
@@ -108,22 +110,20 @@ __device__ __forceinline__ void mlp_split_chunk(const uint32_t (&r)[32], const f
   }
 }
 
-// Adds the team helpers' raw sums of one chunk (32 floats of a row, at
-// src + j * stride for helper j + 1) to r, in member order.
-__device__ __forceinline__ void mlp_merge_chunk(uint32_t (&r)[32], const float* src, size_t stride, int helpers) {
-#pragma unroll 1
-  for (int j = 0; j < helpers; ++j) {
-    const float4* s4 = reinterpret_cast<const float4*>(src + (size_t)j * stride);
-    float4 v4[8];
+// The team helper's raw sums of one chunk (32 floats of a row), loaded ahead
+// of their use, and added to r.
+__device__ __forceinline__ void mlp_load_partial(float4 (&v4)[8], const float* src) {
+  const float4* s4 = reinterpret_cast<const float4*>(src);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) v4[i] = __ldcg(s4 + i);
+  for (int i = 0; i < 8; ++i) v4[i] = __ldcg(s4 + i);
+}
+__device__ __forceinline__ void mlp_add_partial(uint32_t (&r)[32], const float4 (&v4)[8]) {
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      r[4 * i + 0] = __float_as_uint(__fadd_rn(__uint_as_float(r[4 * i + 0]), v4[i].x));
-      r[4 * i + 1] = __float_as_uint(__fadd_rn(__uint_as_float(r[4 * i + 1]), v4[i].y));
-      r[4 * i + 2] = __float_as_uint(__fadd_rn(__uint_as_float(r[4 * i + 2]), v4[i].z));
-      r[4 * i + 3] = __float_as_uint(__fadd_rn(__uint_as_float(r[4 * i + 3]), v4[i].w));
-    }
+  for (int i = 0; i < 8; ++i) {
+    r[4 * i + 0] = __float_as_uint(__fadd_rn(__uint_as_float(r[4 * i + 0]), v4[i].x));
+    r[4 * i + 1] = __float_as_uint(__fadd_rn(__uint_as_float(r[4 * i + 1]), v4[i].y));
+    r[4 * i + 2] = __float_as_uint(__fadd_rn(__uint_as_float(r[4 * i + 2]), v4[i].z));
+    r[4 * i + 3] = __float_as_uint(__fadd_rn(__uint_as_float(r[4 * i + 3]), v4[i].w));
   }
 }
 
@@ -153,7 +153,7 @@ struct TcMlpTeam {
   int pad;
 };
 
-constexpr int kTcMlpMaxTeam = 4;
+constexpr int kTcMlpMaxTeam = 2;
 constexpr int kTcMlpTeamFlagWords = 160;  // 2 x tiles (<= 74) + the departure counter, rounded
 
 // p1: layer 1 (M, K = K1, N = N1, bias, epi); p2: layer 2 (K = N1, N = N2,
@@ -470,16 +470,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
         asm volatile("bar.sync 1, 128;" ::: "memory");
         if (!(ok = *team_ok != 0)) break;
       }
-      // the helpers' sums of this thread's row, chunk c at 32 c
-      const float* hrow = team.ws + ((size_t)(u * (S - 1) * 2 + (int)rank) * 128 + row) * 256;
-      const size_t hstride = (size_t)2 * 128 * 256;  // from one member's sums to the next
+      // the helper's sums of this thread's row (chunk c at 32 c), each chunk
+      // loaded while the one before it is converted
+      const float* hrow = team.ws + ((size_t)(u * 2 + (int)rank) * 128 + row) * 256;
+      float4 pn[8];
+      if (teamed) mlp_load_partial(pn, hrow);
       __syncwarp();
       FTB_TMEM_LD32(tmem + lanes, r);
       FTB_TMEM_WAIT_LD32(r);
       for (int c = 0; c < nch; ++c) {
         const uint32_t gc = g + (uint32_t)c, qs = gc & 3u, use = gc >> 2;
         uint32_t hi[32], lo[32];
-        if (teamed) mlp_merge_chunk(r, hrow + 32 * c, hstride, S - 1);
+        if (teamed) {
+          mlp_add_partial(r, pn);
+          if (c + 1 < nch) mlp_load_partial(pn, hrow + 32 * (c + 1));
+        }
         const float* b = b1s + 32 * c;
         if (ep_bias && ep_relu) mlp_split_chunk<true, true>(r, b, hi, lo);
         else if (ep_bias) mlp_split_chunk<true, false>(r, b, hi, lo);
@@ -570,9 +575,9 @@ inline bool tc_mlp_supported(const TcArgs& t1, const TcWeights& w1, const TcArgs
   return true;
 }
 
-// Team size for `tiles` tiles of layer 1 with nk1 k-blocks: split when at
-// least two pairs per tile are free, at most four, each member keeping at
-// least eight k-blocks.
+// Team size for `tiles` tiles of layer 1 with nk1 k-blocks: two pairs per
+// tile when the tiles leave that many free, each member keeping at least
+// eight k-blocks.
 inline int tc_mlp_team_size(int64_t tiles, int nk1, int max_pairs) {
   if (tiles <= 0) return 1;
   int S = (int)std::min<int64_t>(kTcMlpMaxTeam, max_pairs / tiles);

@@ -129,9 +129,9 @@ FORGETUNE_EXPORT int ftb_model_set_policy(void* model, int policy);
  * in a fixed order), 1 = one SM per tile, 4 = this step and the next GEMM in
  * one launch with this step's output kept in tensor memory (where the step
  * pair qualifies: `mlp_step` in ftb_describe_blob's output; else as 0),
- * 5 = the same, with this step's k-blocks split over a team of 2-4 pairs per
- * tile when the tiles leave at least two pairs each free (the helpers' sums
- * are added to the owner's in member order);
+ * 5 = the same, with this step's k-blocks split over a team of two pairs per
+ * tile when the tiles leave a second pair each free (the helper's sums are
+ * added to the owner's);
  * 0 = chosen by shape (may pick split-K, or the two-layer launch, split over
  * teams when the tiles are few, when neither step carries a configuration).
  * fuse_head: compute a following small-N head in the epilogue.
