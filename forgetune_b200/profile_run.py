@@ -40,7 +40,7 @@ def main(argv=None) -> int:
     builder, shape, _ = workloads.WORKLOADS[args.workload]
     model = builder()
     B = args.batch
-    ir = export_to_ir(model, (torch.zeros((2,) + tuple(shape)),), dynamic_batch=True, max_batch_size=B)
+    ir = export_to_ir(model, (torch.zeros((2,) + tuple(shape)),), dynamic_batch=True, max_batch_size=max(B, 2))
     eng = _native.EngineModel(serialize(ir, enable_fusion=True, bias_first_fused=True, kernel_policy=args.policy))
     dev = torch.cuda.current_device()
     eng.set_devices([dev])
