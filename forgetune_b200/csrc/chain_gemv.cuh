@@ -10,8 +10,9 @@
 // for every CTA after a grid-wide barrier, so the next layer reads them.
 //
 // At the start every warp prefetches into L2 the weight rows it will read in
-// every layer (they do not depend on the activations), so after a barrier a
-// layer waits on L2, not HBM.  Per layer, a warp owns an output column n at
+// every layer (they do not depend on the activations), and before each
+// barrier the next layer's rows into L1, so after a barrier a layer waits
+// only on its input rows.  Per layer, a warp owns an output column n at
 // a time and reads W's column as the contiguous row n of an fp32 [N, K] copy
 // of the weights (float4 loads, eight per lane in flight); the CTA stages the layer's
 // input rows [M, K] in shared memory once (L2 loads: the rows were written
@@ -76,8 +77,8 @@ __device__ __forceinline__ bool chain_grid_sync(unsigned long long* bar, int* er
   __syncthreads();
   if (threadIdx.x == 0) {
     int ok = 1;
-    __threadfence();  // this CTA's stores (ordered before by the CTA barrier) before the arrival
-    atomicAdd(bar, 1ull);
+    // the arrival releases this CTA's stores (ordered before it by the CTA barrier)
+    asm volatile("red.release.gpu.global.add.u64 [%0], 1;" ::"l"(bar) : "memory");
     const unsigned long long target = (unsigned long long)(b + 1) * gridDim.x;
     const unsigned long long t0 = chain_now();
     for (;;) {
@@ -177,7 +178,17 @@ __global__ void __launch_bounds__(kChainWarps * 32, 1) chain_gemv_kernel(const _
         L.y[m * N + n] = v;
       }
     }
-    if (l + 1 < p.n_layers) ok = chain_grid_sync(p.bar, p.err, l, &ok_smem);
+    if (l + 1 < p.n_layers) {
+      // the next layer's weight rows of this warp into L1 while the barrier waits
+      const ChainLayer& Ln = p.layer[l + 1];
+      const size_t row_bytes = (size_t)Ln.K * 4;
+      for (int n = gw; n < Ln.N; n += nw) {
+        const char* row = reinterpret_cast<const char*>(Ln.w) + (size_t)n * row_bytes;
+        for (size_t b = (size_t)lane * 128; b < row_bytes; b += 32 * 128)
+          asm volatile("prefetch.global.L1 [%0];" ::"l"(row + b));
+      }
+      ok = chain_grid_sync(p.bar, p.err, l, &ok_smem);
+    }
   }
   // departure: the last CTA out resets both counters for the next launch
   __syncthreads();

@@ -110,12 +110,12 @@ __device__ __forceinline__ void mlp_split_chunk(const uint32_t (&r)[32], const f
   }
 }
 
-// The team helper's raw sums of one chunk (32 floats of a row), loaded ahead
-// of their use, and added to r.
-__device__ __forceinline__ void mlp_load_partial(float4 (&v4)[8], const float* src) {
-  const float4* s4 = reinterpret_cast<const float4*>(src);
+// The team helper's raw sums of one chunk (32 floats of a row: float4
+// group i at src[i * 128], rows adjacent), loaded ahead of their use, and
+// added to r.
+__device__ __forceinline__ void mlp_load_partial(float4 (&v4)[8], const float4* src) {
 #pragma unroll
-  for (int i = 0; i < 8; ++i) v4[i] = __ldcg(s4 + i);
+  for (int i = 0; i < 8; ++i) v4[i] = __ldcg(src + i * 128);
 }
 __device__ __forceinline__ void mlp_add_partial(uint32_t (&r)[32], const float4 (&v4)[8]) {
 #pragma unroll
@@ -146,7 +146,7 @@ struct TcMlpSmem {
 
 // Split of layer 1 over a team of pairs (S = 1: no split).
 struct TcMlpTeam {
-  float* ws;         // helper sums: [((tile (S-1) + s-1) 2 + rank) 128 + row] x 256 floats
+  float* ws;         // helper sums: per tile and CTA rank 128 rows x 256 columns, as [chunk][group of 4][row] float4s
   unsigned* flags;   // [2 tiles]: helper CTAs that published their sums, per tile and CTA rank
   unsigned* depart;  // CTAs that left the launch
   int S;
@@ -421,16 +421,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
       const int row = q * 32 + lane;  // this thread's row of the CTA's 128
       if (!owner) {
         // helper: publish this CTA's raw layer-1 sums, then count them in
-        float* dst = team.ws + ((size_t)((u * (S - 1) + member - 1) * 2 + (int)rank) * 128 + row) * 256;
+        // layout [chunk][float4 group][row] of float4s: a warp's store is 512
+        // contiguous bytes (its 32 rows' group i), and so is the owner's load
+        float4* dst = reinterpret_cast<float4*>(team.ws + (size_t)(u * 2 + (int)rank) * 128 * 256) + row;
         for (int c = 0; c < nch; ++c) {
           __syncwarp();
           FTB_TMEM_LD32(tmem + lanes + (uint32_t)(32 * c), r);
           FTB_TMEM_WAIT_LD32(r);
-          float4* d4 = reinterpret_cast<float4*>(dst + 32 * c);
 #pragma unroll
           for (int i = 0; i < 8; ++i)
-            d4[i] = make_float4(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1]),
-                                __uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3]));
+            dst[(c * 8 + i) * 128] = make_float4(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1]),
+                                                 __uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3]));
         }
         tc_fence_before();
         asm volatile("bar.sync 1, 128;" ::: "memory");
@@ -472,7 +473,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
       }
       // the helper's sums of this thread's row (chunk c at 32 c), each chunk
       // loaded while the one before it is converted
-      const float* hrow = team.ws + ((size_t)(u * 2 + (int)rank) * 128 + row) * 256;
+      const float4* hrow = reinterpret_cast<const float4*>(team.ws + (size_t)(u * 2 + (int)rank) * 128 * 256) + row;
       float4 pn[8];
       if (teamed) mlp_load_partial(pn, hrow);
       __syncwarp();
@@ -483,7 +484,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
         uint32_t hi[32], lo[32];
         if (teamed) {
           mlp_add_partial(r, pn);
-          if (c + 1 < nch) mlp_load_partial(pn, hrow + 32 * (c + 1));
+          if (c + 1 < nch) mlp_load_partial(pn, hrow + (c + 1) * 8 * 128);
         }
         const float* b = b1s + 32 * c;
         if (ep_bias && ep_relu) mlp_split_chunk<true, true>(r, b, hi, lo);
