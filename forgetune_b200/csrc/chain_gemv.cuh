@@ -80,17 +80,17 @@ __device__ __forceinline__ bool chain_grid_sync(unsigned long long* bar, int* er
     // the arrival releases this CTA's stores (ordered before it by the CTA barrier)
     asm volatile("red.release.gpu.global.add.u64 [%0], 1;" ::"l"(bar) : "memory");
     const unsigned long long target = (unsigned long long)(b + 1) * gridDim.x;
+    // poll without sleeping (a sleep's granularity is coarser than the wait)
     const unsigned long long t0 = chain_now();
-    for (;;) {
+    for (uint32_t it = 0;; ++it) {
       unsigned long long v;
       asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(bar) : "memory");
       if (v >= target) break;
-      if (chain_now() - t0 > kChainWaitNs) {
+      if ((it & 15u) == 15u && chain_now() - t0 > kChainWaitNs) {
         atomicCAS(err, 0, 20 + b);
         ok = 0;
         break;
       }
-      __nanosleep(64);
     }
     __threadfence();
     *ok_smem = ok;

@@ -14,16 +14,17 @@
 //   warp 1     TMEM (two accumulators of BN columns) and the MMAs (one
 //              elected lane, tcgen05.mma kind::tf32 M=128 N=BN K=8, three
 //              per k-step);
-//   warps 2-5  the gather: thread t owns pixel m0 + t of the tile and, per
-//              k-block, issues its 16 input loads at once (zero padding
-//              decided per value from a k-table of {ci H W + kh dh W + kw dw,
-//              kh dh, kw dw} staged in shared memory; a value outside the
-//              image loads a valid address and is zeroed by a mask), splits
-//              them into tf32 hi and lo and writes both rows
-//              in the layout TMA's 64-byte swizzle produces (16-byte chunk c
-//              of row r at chunk position c ^ ((r >> 1) & 3)); the next
-//              k-block's values are loaded while this one is written;
-//   warps 6-9  epilogue, overlapping the next tile's MMAs: tcgen05.ld (lane =
+//   warps 2-17 the gather (four warps per scheduler, to hide load latency):
+//              thread (r, h) owns pixel m0 + r of the tile and k-chunk h (4 k)
+//              of every k-block; it issues its 4 input loads at once (zero
+//              padding decided per value from a k-table of {ci H W + kh dh W
+//              + kw dw, kh dh, kw dw} staged in shared memory; a value outside
+//              the image loads a valid address and is zeroed by a mask),
+//              splits them into tf32 hi and lo and writes both 16-byte chunks
+//              in the layout TMA's 64-byte swizzle produces (chunk c of row r
+//              at chunk position c ^ ((r >> 1) & 3)); the next two k-blocks'
+//              values are loaded while this one is written;
+//   warps 18-21 epilogue, overlapping the next tile's MMAs: tcgen05.ld (lane =
 //              pixel, 32 channels), bias / ReLU / residual in registers, and
 //              stores straight to NCHW (for one channel the 32 pixels of a
 //              warp are consecutive addresses of one plane).
@@ -60,38 +61,39 @@ struct TcConvSmem {
   static constexpr int TOTAL = 1024 + STAGES * STAGE_BYTES + BAR_BYTES + KTAB_BYTES;
 };
 
-// Issues the 16 loads of col(m, kb*16 .. kb*16+15) for this thread's pixel
-// at once: the k-table comes from shared memory, a value outside the image
-// (or past K) loads the image's first element instead and is zeroed later by
-// its bit in *valid, so no load waits on another.
-__device__ __forceinline__ void conv_gather16(float (&v)[16], uint32_t* valid, const int4* ktab_s, int K, int H,
-                                              int W, const float* xb, int ih0, int iw0, bool live, int kb) {
+constexpr int kConvGatherWarps = 16;                   // 4 per scheduler: latency hiding for the gather
+constexpr int kConvThreads = (2 + kConvGatherWarps + 4) * 32;  // producer, MMA, gather, epilogue
+
+// Issues the 4 loads of col(m, k0 .. k0+3) for this thread's pixel at once:
+// the k-table comes from shared memory, a value outside the image (or past
+// K) loads the image's first element instead and is zeroed later by its bit
+// in the returned mask, so no load waits on another.
+__device__ __forceinline__ uint32_t conv_gather4(float4& v, const int4* ktab_s, int K, int H, int W, const float* xb,
+                                                 int ih0, int iw0, bool live, int k0) {
   uint32_t ok = 0;
+  float t[4];
 #pragma unroll
-  for (int j = 0; j < 16; ++j) {
-    const int k = kb * 16 + j;
+  for (int j = 0; j < 4; ++j) {
+    const int k = k0 + j;
     const int4 e = ktab_s[k < K ? k : 0];
     const int ih = ih0 + e.y, iw = iw0 + e.z;
     const bool in = live && k < K && ih >= 0 && ih < H && iw >= 0 && iw < W;
     const float* a = in ? xb + ((ptrdiff_t)ih0 * W + iw0 + e.x) : xb;
-    v[j] = __ldg(a);
+    t[j] = __ldg(a);
     ok |= (in ? 1u : 0u) << j;
   }
-  *valid = ok;
+  v = make_float4(t[0], t[1], t[2], t[3]);
+  return ok;
 }
 
-// Row r (64 bytes) of a 64-byte-swizzled k-block tile: chunk c at c ^ ((r >> 1) & 3).
-__device__ __forceinline__ void conv_store_row(uint8_t* tile, int r, const float (&h)[16]) {
-  const int sw = (r >> 1) & 3;
-#pragma unroll
-  for (int c = 0; c < 4; ++c) {
-    float4* d = reinterpret_cast<float4*>(tile + r * 64 + ((c ^ sw) << 4));
-    *d = make_float4(h[4 * c], h[4 * c + 1], h[4 * c + 2], h[4 * c + 3]);
-  }
+// 16-byte chunk c of row r of a 64-byte-swizzled k-block tile (rows of 64
+// bytes): it sits at chunk position c ^ ((r >> 1) & 3).
+__device__ __forceinline__ void conv_store_chunk(uint8_t* tile, int r, int c, float4 v) {
+  *reinterpret_cast<float4*>(tile + r * 64 + ((c ^ ((r >> 1) & 3)) << 4)) = v;
 }
 
 template <int BN, int STAGES>
-__global__ void __launch_bounds__(kTcThreads, 1)
+__global__ void __launch_bounds__(kConvThreads, 1)
     tc_conv_kernel(const __grid_constant__ CUtensorMap map_bhi, const __grid_constant__ CUtensorMap map_blo,
                    TcConvParams p) {
   using L = TcConvSmem<BN, STAGES>;
@@ -105,7 +107,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   auto blo_tile = [&](int s) { return smem + s * L::STAGE_BYTES + 2 * L::A_BYTES + L::B_BYTES; };
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * L::STAGE_BYTES);
   uint64_t* full = bars;                // W k-block landed
-  uint64_t* conv = bars + STAGES;       // A gathered and split (4 arrivals)
+  uint64_t* conv = bars + STAGES;       // A gathered and split (one arrival per gather warp)
   uint64_t* empty = bars + 2 * STAGES;  // MMAs done reading the stage
   uint64_t* accf = bars + 3 * STAGES;   // [2] accumulator complete
   uint64_t* acce = accf + 2;            // [2] accumulator drained (4 arrivals)
@@ -126,7 +128,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&conv[s], 4);
+      mbar_init(&conv[s], kConvGatherWarps);
       mbar_init(&empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -152,9 +154,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   grid_dep_trigger();
   const uint32_t tmem = *tmem_slot;
   // the gather warps stage the k-table (a weight-side constant, K <= KTAB_MAX)
-  if (warp >= 2 && warp < 6) {
-    for (int k = threadIdx.x - 64; k < p.K; k += 128) ktab_s[k] = __ldg(p.ktab + k);
-    asm volatile("bar.sync 2, 128;" ::: "memory");
+  if (warp >= 2 && warp < 2 + kConvGatherWarps) {
+    for (int k = threadIdx.x - 64; k < p.K; k += kConvGatherWarps * 32) ktab_s[k] = __ldg(p.ktab + k);
+    asm volatile("bar.sync 2, %0;" ::"n"(kConvGatherWarps * 32) : "memory");
   }
 
   if (warp == 0) {
@@ -214,9 +216,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       __syncwarp();
       mbar_wait_warp(drain, 0, abort_flag, p.err, 5, /*ignore_abort=*/true);
     }
-  } else if (warp < 6) {
-    // warps 2..5: gather, split, store; the next k-block's loads in flight
-    const int r = threadIdx.x - 64;  // this thread's pixel row of the tile
+  } else if (warp < 2 + kConvGatherWarps) {
+    // gather warps: thread (r, h) writes k-chunk h (4 k) of pixel row r of
+    // every k-block; the next two k-blocks' loads are in flight meanwhile
+    // (the pixel's geometry is computed once per tile: the gather is bound
+    // by its instruction count, so a per-load index computation costs more
+    // than the cross-tile prefetch it would buy)
+    const int gt = threadIdx.x - 64;
+    const int r = gt & (kTcBM - 1);  // pixel row of the tile
+    const int h = gt >> 7;           // 16-byte chunk of the 64-byte k-block row
     uint32_t it = 0;
     bool ok = true;
     for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
@@ -227,32 +235,35 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       const int oh = pp / p.Wo, ow = pp - oh * p.Wo;
       const int ih0 = oh * p.sh - p.ph, iw0 = ow * p.sw - p.pw;
       const float* xb = p.x + (size_t)b * p.Cin * p.H * p.W;
-      float cur[16], nxt[16];
-      uint32_t vcur = 0, vnxt = 0;
-      conv_gather16(cur, &vcur, ktab_s, p.K, p.H, p.W, xb, ih0, iw0, live, 0);
+      float4 v0, v1, v2;
+      uint32_t m0 = conv_gather4(v0, ktab_s, p.K, p.H, p.W, xb, ih0, iw0, live, 4 * h);
+      uint32_t m1 = nk > 1 ? conv_gather4(v1, ktab_s, p.K, p.H, p.W, xb, ih0, iw0, live, 16 + 4 * h) : 0u;
       for (int kb = 0; kb < nk; ++kb, ++it) {
-        if (kb + 1 < nk) conv_gather16(nxt, &vnxt, ktab_s, p.K, p.H, p.W, xb, ih0, iw0, live, kb + 1);
-        float h[16], l[16];
+        uint32_t m2 = 0;
+        if (kb + 2 < nk) m2 = conv_gather4(v2, ktab_s, p.K, p.H, p.W, xb, ih0, iw0, live, (kb + 2) * 16 + 4 * h);
+        const float c[4] = {m0 & 1u ? v0.x : 0.0f, m0 & 2u ? v0.y : 0.0f, m0 & 4u ? v0.z : 0.0f,
+                            m0 & 8u ? v0.w : 0.0f};
+        float hi[4], lo[4];
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const float c = (vcur >> j) & 1u ? cur[j] : 0.0f;
-          h[j] = tf32_rna(c);
-          l[j] = tf32_rna(c - h[j]);
+        for (int j = 0; j < 4; ++j) {
+          hi[j] = tf32_rna(c[j]);
+          lo[j] = tf32_rna(c[j] - hi[j]);
         }
         const int s = (int)(it % STAGES);
         if (!(ok = mbar_wait_warp(&full[s], (it / STAGES) & 1u, abort_flag, p.err, 6))) break;
-        conv_store_row(a_tile(s), r, h);
-        conv_store_row(alo_tile(s), r, l);
+        conv_store_chunk(a_tile(s), r, h, make_float4(hi[0], hi[1], hi[2], hi[3]));
+        conv_store_chunk(alo_tile(s), r, h, make_float4(lo[0], lo[1], lo[2], lo[3]));
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(&conv[s]);
-#pragma unroll
-        for (int j = 0; j < 16; ++j) cur[j] = nxt[j];
-        vcur = vnxt;
+        v0 = v1;
+        m0 = m1;
+        v1 = v2;
+        m1 = m2;
       }
     }
   } else {
-    // warps 6..9: epilogue, one TMEM lane quarter (32 pixels) each
+    // the last four warps: epilogue, one TMEM lane quarter (32 pixels) each
     const int q = warp & 3;
     const uint32_t lanes = (uint32_t)(q * 32) << 16;
     const bool bias = p.bias != nullptr && (p.epi & EPI_BIAS_LAST);
@@ -311,7 +322,7 @@ inline int launch_tc_conv_bn(TcConvParams p, const TcWeights& w, int sm_count, c
   const int64_t ntiles = ((int64_t)(p.M + kTcBM - 1) / kTcBM) * ((p.N + BN - 1) / BN);
   const unsigned grid = (unsigned)std::min<int64_t>(ntiles, sm_count);
   const int bi = tc_bn_index(BN);
-  return note_launch(pdl_launch(tc_conv_kernel<BN, STAGES>, dim3(grid), dim3(kTcThreads), L::TOTAL, s,
+  return note_launch(pdl_launch(tc_conv_kernel<BN, STAGES>, dim3(grid), dim3(kConvThreads), L::TOTAL, s,
                                 w.map_hi[1][bi], w.map_lo[1][bi], p));
 }
 
