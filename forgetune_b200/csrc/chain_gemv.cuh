@@ -9,12 +9,15 @@
 // a cooperative launch) walks the layers; a layer's outputs are complete
 // for every CTA after a grid-wide barrier, so the next layer reads them.
 //
-// At the start every warp prefetches into L2 the weight rows it will read in
-// every layer (they do not depend on the activations), and before each
-// barrier the next layer's rows into L1, so after a barrier a layer waits
-// only on its input rows.  Per layer, a warp owns an output column n at
-// a time and reads W's column as the contiguous row n of an fp32 [N, K] copy
-// of the weights (float4 loads, eight per lane in flight); the CTA stages the layer's
+// On B200 a dependent L2 round trip costs about 0.6 us (a probe with
+// %globaltimer stamps per phase), so the kernel keeps them off each layer's
+// critical path: at the start every warp copies the weight rows it will read
+// in every layer into shared memory (cp.async, one group per layer; when
+// they do not fit, it prefetches them into L2, and into L1 before each
+// barrier), and a column's bias and residual are loaded together with its
+// weights.  Per layer, a warp owns an output column n at a time and reads
+// W's column as the contiguous row n of an fp32 [N, K] copy of the weights
+// (float4 loads, eight per lane in flight); the CTA stages the layer's
 // input rows [M, K] in shared memory once (L2 loads: the rows were written
 // by other SMs in this launch).  Each lane accumulates its k = 4 lane + 128 i
 // terms for all M rows; the 32 lane sums of a value are added by a butterfly
@@ -33,6 +36,8 @@
 
 #include <cuda_runtime.h>
 
+#include <algorithm>
+#include <atomic>
 #include <cstdint>
 
 #include "epilogue.cuh"
@@ -42,7 +47,7 @@ namespace ftb {
 constexpr int kChainMaxLayers = 24;
 constexpr int kChainMaxRows = 16;
 constexpr int kChainWarps = 8;
-constexpr int kChainSmemBytes = 160 * 1024;  // staged input rows: M x K floats
+constexpr int kChainSmemBytes = 220 * 1024;  // input rows (M x K floats) and cached weight rows
 constexpr unsigned long long kChainWaitNs = 2000000000ull;
 
 struct ChainLayer {
@@ -62,6 +67,8 @@ struct ChainParams {
   unsigned long long* bar;  // [0] arrivals, [1] departures; zero between launches
   int* err;                 // the replica's error word (mapped host memory)
   int stall_test;           // failure-detection hook: CTA 0 never arrives at the first barrier
+  int xs_floats;            // shared memory for the input rows (floats, a multiple of 4)
+  int wcache_per_warp;      // floats of cached weight rows per warp after them (0 = rows stream from L2)
   int pad;
   ChainLayer layer[kChainMaxLayers];
 };
@@ -99,59 +106,102 @@ __device__ __forceinline__ bool chain_grid_sync(unsigned long long* bar, int* er
   return *ok_smem != 0;
 }
 
+__device__ __forceinline__ void chain_cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
+               : "memory");
+}
+// cp.async.wait_group takes an immediate: wait until at most `pending` of
+// this thread's newest groups are still in flight (more than 7: wait for 7)
+__device__ __forceinline__ void chain_cp_wait(int pending) {
+  switch (pending) {
+    case 0: asm volatile("cp.async.wait_group 0;" ::: "memory"); break;
+    case 1: asm volatile("cp.async.wait_group 1;" ::: "memory"); break;
+    case 2: asm volatile("cp.async.wait_group 2;" ::: "memory"); break;
+    case 3: asm volatile("cp.async.wait_group 3;" ::: "memory"); break;
+    case 4: asm volatile("cp.async.wait_group 4;" ::: "memory"); break;
+    case 5: asm volatile("cp.async.wait_group 5;" ::: "memory"); break;
+    case 6: asm volatile("cp.async.wait_group 6;" ::: "memory"); break;
+    default: asm volatile("cp.async.wait_group 7;" ::: "memory"); break;
+  }
+}
+
+// MB: rows compiled for (M <= MB): the unrolled row loops and the code a
+// warp fetches and issues scale with the batch, not with the largest one.
+template <int MB>
 __global__ void __launch_bounds__(kChainWarps * 32, 1) chain_gemv_kernel(const __grid_constant__ ChainParams p) {
-  extern __shared__ float4 chain_xs[];  // [M][K/4] of the current layer
+  extern __shared__ float4 chain_smem[];
+  float4* chain_xs = chain_smem;  // [M][K/4] of the current layer
   __shared__ int ok_smem;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int gw = blockIdx.x * kChainWarps + warp;
   const int nw = gridDim.x * kChainWarps;
-  const int M = p.M;
+  const int M = p.M, NL = p.n_layers;
+  const bool cached = p.wcache_per_warp > 0;
+  float* wcache = reinterpret_cast<float*>(chain_smem) + p.xs_floats + (size_t)warp * p.wcache_per_warp;
   bool ok = !(p.stall_test && blockIdx.x == 0);  // the hook: CTA 0 leaves without arriving
-  // Every layer's weight rows this warp will read, prefetched into L2 now:
-  // they do not depend on the activations, so later layers find them there
-  // instead of waiting on HBM after each barrier.
-  for (int l = 0; l < p.n_layers && ok; ++l) {
-    const ChainLayer& L = p.layer[l];
-    const size_t row_bytes = (size_t)L.K * 4;
-    for (int n = gw; n < L.N; n += nw) {
-      const char* row = reinterpret_cast<const char*>(L.w) + (size_t)n * row_bytes;
-      for (size_t b = (size_t)lane * 128; b < row_bytes; b += 32 * 128)
-        asm volatile("prefetch.global.L2 [%0];" ::"l"(row + b));
+  // This warp's weight rows of every layer: copied into shared memory now
+  // (one cp.async group per layer, layer 0's first), or, when they do not
+  // fit, prefetched into L2.  They do not depend on the activations, so a
+  // layer after a barrier waits only on its input rows.
+  {
+    int off = 0;
+    for (int l = 0; l < NL && ok; ++l) {
+      const ChainLayer& L = p.layer[l];
+      const int K4 = L.K >> 2;
+      for (int n = gw; n < L.N; n += nw) {
+        if (cached) {
+          const float4* src = reinterpret_cast<const float4*>(L.w) + (size_t)n * K4;
+          for (int k4 = lane; k4 < K4; k4 += 32) chain_cp_async16(wcache + off + 4 * k4, src + k4);
+          off += L.K;
+        } else {
+          const char* row = reinterpret_cast<const char*>(L.w) + (size_t)n * L.K * 4;
+          for (int b = lane * 128; b < L.K * 4; b += 32 * 128) asm volatile("prefetch.global.L2 [%0];" ::"l"(row + b));
+        }
+      }
+      if (cached) asm volatile("cp.async.commit_group;" ::: "memory");
     }
   }
-  for (int l = 0; l < p.n_layers && ok; ++l) {
+  int woff = 0;
+  for (int l = 0; l < NL && ok; ++l) {
     const ChainLayer& L = p.layer[l];
     const int K4 = L.K >> 2, N = L.N;
     const float4* a4 = reinterpret_cast<const float4*>(L.a);
     for (int i = threadIdx.x; i < M * K4; i += blockDim.x) chain_xs[i] = __ldcg(a4 + i);
-    __syncthreads();
-    for (int n = gw; n < N; n += nw) {
-      const float4* w4 = reinterpret_cast<const float4*>(L.w) + (size_t)n * K4;
-      float acc[kChainMaxRows];
+    if (cached) chain_cp_wait(NL - 1 - l);  // this thread's copies of this layer's rows have landed
+    __syncthreads();                         // (and every other thread's, and the input rows)
+    int j = 0;
+    for (int n = gw; n < N; n += nw, ++j) {
+      const float4* w4 = cached ? reinterpret_cast<const float4*>(wcache + woff + j * L.K)
+                                : reinterpret_cast<const float4*>(L.w) + (size_t)n * K4;
+      // the epilogue's operands are loaded with the weights, not after the sums
+      const int64_t mrow = lane < M ? lane : 0;
+      const float bv = L.bias ? ((L.epi & EPI_BIAS_ROWS) ? __ldg(L.bias + mrow * N + n) : __ldg(L.bias + n)) : 0.0f;
+      const float rv = (L.epi & EPI_RESIDUAL) ? __ldcg(L.res + mrow * N + n) : 0.0f;
+      float acc[MB];
 #pragma unroll
-      for (int m = 0; m < kChainMaxRows; ++m) acc[m] = 0.0f;
+      for (int m = 0; m < MB; ++m) acc[m] = 0.0f;
       // eight float4 of the row per lane in flight at once (K <= 1024 in one round)
       constexpr int WB = 8;
       for (int kb = 0; kb < K4; kb += 32 * WB) {
         float4 wv[WB];
 #pragma unroll
-        for (int j = 0; j < WB; ++j) {
-          const int k4 = kb + 32 * j + lane;
-          wv[j] = k4 < K4 ? __ldg(w4 + k4) : make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int q = 0; q < WB; ++q) {
+          const int k4 = kb + 32 * q + lane;
+          wv[q] = k4 < K4 ? (cached ? w4[k4] : __ldg(w4 + k4)) : make_float4(0.f, 0.f, 0.f, 0.f);
         }
 #pragma unroll
-        for (int j = 0; j < WB; ++j) {
-          const int k4 = kb + 32 * j + lane;
+        for (int q = 0; q < WB; ++q) {
+          const int k4 = kb + 32 * q + lane;
           if (k4 < K4) {
 #pragma unroll
-            for (int m = 0; m < kChainMaxRows; ++m) {
+            for (int m = 0; m < MB; ++m) {
               if (m < M) {
                 const float4 xv = chain_xs[m * K4 + k4];
                 float s = acc[m];
-                s = fmaf(xv.x, wv[j].x, s);
-                s = fmaf(xv.y, wv[j].y, s);
-                s = fmaf(xv.z, wv[j].z, s);
-                s = fmaf(xv.w, wv[j].w, s);
+                s = fmaf(xv.x, wv[q].x, s);
+                s = fmaf(xv.y, wv[q].y, s);
+                s = fmaf(xv.z, wv[q].z, s);
+                s = fmaf(xv.w, wv[q].w, s);
                 acc[m] = s;
               }
             }
@@ -160,7 +210,7 @@ __global__ void __launch_bounds__(kChainWarps * 32, 1) chain_gemv_kernel(const _
       }
       float mine = 0.0f;  // lane m keeps row m's sum
 #pragma unroll
-      for (int m = 0; m < kChainMaxRows; ++m) {
+      for (int m = 0; m < MB; ++m) {
         if (m < M) {
           float v = acc[m];
 #pragma unroll
@@ -169,27 +219,30 @@ __global__ void __launch_bounds__(kChainWarps * 32, 1) chain_gemv_kernel(const _
         }
       }
       if (lane < M) {
-        const int64_t m = lane;
         float v = mine;
-        if (L.bias) v = __fadd_rn(v, (L.epi & EPI_BIAS_ROWS) ? __ldg(L.bias + m * N + n) : __ldg(L.bias + n));
+        if (L.bias) v = __fadd_rn(v, bv);
         if (L.epi & EPI_RELU_PRE) v = relu_keep_nan(v);
-        if (L.epi & EPI_RESIDUAL) v = __fadd_rn(v, __ldcg(L.res + m * N + n));
+        if (L.epi & EPI_RESIDUAL) v = __fadd_rn(v, rv);
         if (L.epi & EPI_RELU_POST) v = relu_keep_nan(v);
-        L.y[m * N + n] = v;
+        L.y[mrow * N + n] = v;
       }
     }
-    if (l + 1 < p.n_layers) {
-      // the next layer's weight rows of this warp into L1 while the barrier waits
-      const ChainLayer& Ln = p.layer[l + 1];
-      const size_t row_bytes = (size_t)Ln.K * 4;
-      for (int n = gw; n < Ln.N; n += nw) {
-        const char* row = reinterpret_cast<const char*>(Ln.w) + (size_t)n * row_bytes;
-        for (size_t b = (size_t)lane * 128; b < row_bytes; b += 32 * 128)
-          asm volatile("prefetch.global.L1 [%0];" ::"l"(row + b));
+    woff += j * L.K;
+    if (l + 1 < NL) {
+      if (!cached) {
+        // the next layer's weight rows of this warp into L1 while the barrier waits
+        const ChainLayer& Ln = p.layer[l + 1];
+        const size_t row_bytes = (size_t)Ln.K * 4;
+        for (int n = gw; n < Ln.N; n += nw) {
+          const char* row = reinterpret_cast<const char*>(Ln.w) + (size_t)n * row_bytes;
+          for (size_t b = (size_t)lane * 128; b < row_bytes; b += 32 * 128)
+            asm volatile("prefetch.global.L1 [%0];" ::"l"(row + b));
+        }
       }
       ok = chain_grid_sync(p.bar, p.err, l, &ok_smem);
     }
   }
+  if (cached) asm volatile("cp.async.wait_group 0;" ::: "memory");  // nothing in flight into shared memory
   // departure: the last CTA out resets both counters for the next launch
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -202,11 +255,31 @@ __global__ void __launch_bounds__(kChainWarps * 32, 1) chain_gemv_kernel(const _
   }
 }
 
+// Shared memory of a launch over `grid` CTAs: the input rows (M x max K)
+// and, when everything fits, each warp's weight rows of every layer.  Fills
+// p.xs_floats / p.wcache_per_warp; returns the bytes, or 0 when the input
+// rows alone do not fit.
+inline size_t chain_plan(ChainParams& p, int grid) {
+  int kmax = 0;
+  for (int l = 0; l < p.n_layers; ++l) kmax = std::max(kmax, p.layer[l].K);
+  p.xs_floats = (p.M * kmax + 3) / 4 * 4;
+  const size_t base = (size_t)p.xs_floats * 4;
+  if (base > (size_t)kChainSmemBytes) return 0;
+  const int nw = grid * kChainWarps;
+  int64_t per_warp = 0;
+  for (int l = 0; l < p.n_layers; ++l) per_warp += (int64_t)((p.layer[l].N + nw - 1) / nw) * p.layer[l].K;
+  per_warp = (per_warp + 3) / 4 * 4;
+  const int64_t with_cache = (int64_t)base + (int64_t)kChainWarps * per_warp * 4;
+  p.wcache_per_warp = with_cache <= kChainSmemBytes ? (int)per_warp : 0;
+  return p.wcache_per_warp ? (size_t)with_cache : base;
+}
+
 // Launches the chain on `grid` CTAs (cooperative: all co-resident).
 // Returns 0 when launched, -1 on a launch error (kept for take_launch_error).
-inline int launch_chain(const ChainParams& p, int grid, size_t smem, cudaStream_t s) {
+template <int MB>
+inline int launch_chain_mb(const ChainParams& p, int grid, size_t smem, cudaStream_t s) {
   static std::atomic<uint64_t> attr{0};
-  cudaError_t e = smem_limit_once(chain_gemv_kernel, kChainSmemBytes, attr);
+  cudaError_t e = smem_limit_once(chain_gemv_kernel<MB>, kChainSmemBytes, attr);
   if (e != cudaSuccess) return note_launch(e);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)grid);
@@ -218,7 +291,15 @@ inline int launch_chain(const ChainParams& p, int grid, size_t smem, cudaStream_
   attrs[0].val.cooperative = 1;
   cfg.attrs = attrs;
   cfg.numAttrs = 1;
-  return note_launch(cudaLaunchKernelEx(&cfg, chain_gemv_kernel, p));
+  return note_launch(cudaLaunchKernelEx(&cfg, chain_gemv_kernel<MB>, p));
+}
+
+inline int launch_chain(const ChainParams& p, int grid, size_t smem, cudaStream_t s) {
+  if (p.M <= 1) return launch_chain_mb<1>(p, grid, smem, s);
+  if (p.M <= 2) return launch_chain_mb<2>(p, grid, smem, s);
+  if (p.M <= 4) return launch_chain_mb<4>(p, grid, smem, s);
+  if (p.M <= 8) return launch_chain_mb<8>(p, grid, smem, s);
+  return launch_chain_mb<16>(p, grid, smem, s);
 }
 
 }  // namespace ftb

@@ -127,6 +127,8 @@ struct ExecCtx {
   // the copies then run inside the forward's CUDA graph
   float* h_in = nullptr;
   float* h_out = nullptr;
+  float* h_in_dev = nullptr;  // device addresses of the mapped staging buffers
+  float* h_out_dev = nullptr;
   struct CachedGraph {
     int64_t batch;
     const float* in;
@@ -566,6 +568,21 @@ static void copy_floats(const float* a, float* y, int64_t n, int sm, cudaStream_
 // Enqueues the launch list for `batch` rows on stream s.  With `marks`
 // (steps + 1 events) an event is recorded before every step and after the
 // last one, so per-step device times can be read back afterwards.
+// Whether the launch list at this batch runs as the one-launch chain kernel
+// (every condition of enqueue's chain branch that does not depend on the
+// buffers' addresses).
+static bool chain_takes(const Model* m, const Replica* rep, int64_t batch) {
+  const int policy = m->prog.graph.kernel_policy;
+  if (!(policy == KP_AUTO || policy == KP_SIMT) || rep->chain_grid <= 0 || batch < 1 || batch > kChainMaxRows ||
+      (size_t)batch * (size_t)rep->chain_kmax * 4 > (size_t)kChainSmemBytes)
+    return false;
+  for (const Step& st : rep->steps) {
+    const TuneRecord* tr = st.tuned_for(batch);
+    if (tr && tr->family != TF_HEURISTIC) return false;
+  }
+  return true;
+}
+
 static int enqueue(const Model* m, const Replica* rep, ExecCtx* c, const float* in, float* out, int64_t batch,
                    cudaStream_t s, cudaEvent_t* marks = nullptr) {
   char* arena = c->arena;
@@ -608,9 +625,9 @@ static int enqueue(const Model* m, const Replica* rep, ExecCtx* c, const float* 
       L.epi = st.epi;
       if (reinterpret_cast<uintptr_t>(L.a) & 15u) take = false;  // float4 rows
     }
-    if (take) {
+    const size_t smem = take ? chain_plan(p, rep->chain_grid) : 0;
+    if (take && smem > 0) {
       if (marks) cudaEventRecord(marks[0], s);
-      const size_t smem = (size_t)batch * (size_t)rep->chain_kmax * 4;
       if (launch_chain(p, rep->chain_grid, smem, s) != 0) {
         set_error(std::string("chain kernel launch failed: ") + cudaGetErrorString(take_launch_error()));
         return ST_DEVICE;
@@ -1024,18 +1041,32 @@ static int run_host_one(Model* m, int dev, const float* in, float* out, int64_t 
       // small run: host memcpy into pinned staging, one graph launch that
       // copies in, computes and copies out, one synchronisation
       if (!c->h_in) {
-        if (cudaHostAlloc(reinterpret_cast<void**>(&c->h_in), kHostStageBytes, cudaHostAllocDefault) != cudaSuccess ||
-            cudaHostAlloc(reinterpret_cast<void**>(&c->h_out), kHostStageBytes, cudaHostAllocDefault) !=
-                cudaSuccess) {
+        if (cudaHostAlloc(reinterpret_cast<void**>(&c->h_in), kHostStageBytes, cudaHostAllocMapped) != cudaSuccess ||
+            cudaHostAlloc(reinterpret_cast<void**>(&c->h_out), kHostStageBytes, cudaHostAllocMapped) != cudaSuccess ||
+            cudaHostGetDevicePointer(reinterpret_cast<void**>(&c->h_in_dev), c->h_in, 0) != cudaSuccess ||
+            cudaHostGetDevicePointer(reinterpret_cast<void**>(&c->h_out_dev), c->h_out, 0) != cudaSuccess) {
           cudaGetLastError();
           set_error("pinned host staging allocation failed");
           return ST_ALLOC;
         }
       }
       std::memcpy(c->h_in, in, in_b);
-      rc = run_graph(m, rep, c, c->d_in, c->d_out, batch, c->stream, true, in_b, out_b);
+      if (chain_takes(m, rep, batch)) {
+        // the one-launch chain reads its input rows from and writes its
+        // output to the mapped staging buffers itself: no copy at all
+        rc = run_graph(m, rep, c, c->h_in_dev, c->h_out_dev, batch, c->stream);
+      } else {
+        rc = run_graph(m, rep, c, c->d_in, c->d_out, batch, c->stream, true, in_b, out_b);
+      }
       if (rc) return rc;
-      CUDA_TRY(cudaStreamSynchronize(c->stream));
+      // a few microseconds of work: poll instead of sleeping in the driver
+      cudaError_t q;
+      while ((q = cudaStreamQuery(c->stream)) == cudaErrorNotReady) {
+      }
+      if (q != cudaSuccess) {
+        set_error(std::string("small run: ") + cudaGetErrorString(q));
+        return ST_DEVICE;
+      }
       rc = check_kernel_error(rep);
       if (rc) return rc;
       std::memcpy(out, c->h_out, out_b);

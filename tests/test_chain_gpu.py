@@ -1,5 +1,7 @@
 """The small-batch chain kernel: the whole forward pass of a chain of dense
-layers in one launch for at most 16 rows (csrc/chain_gemv.cuh).
+layers in one launch for at most 16 rows (csrc/chain_gemv.cuh), with every
+warp's weight rows cached in shared memory when they fit and streamed from
+L2 otherwise.
 
 * it is the kernel that runs (one kernel per forward) for the tiny and the
   residual MLP at 1..16 rows, and the outputs match the oracle (the
@@ -60,6 +62,21 @@ def test_chain_runs_and_matches_oracle(name, policy, tmp_path):
     # 17 rows: the per-layer kernels again
     got = run_dev(eng, workloads.seeded_input((17,) + tuple(shape)).numpy(), 10)
     assert eng.graph_kernels() > 1 or name == "tiny_mlp"
+    eng.close()
+    cm.close()
+
+
+def test_chain_streams_weights_that_do_not_fit(tmp_path):
+    """Weight rows that do not fit the CTAs' shared memory (2 x 16 MB here)
+    stream from L2 instead of being cached; still the one kernel of the
+    forward, still the oracle's values."""
+    torch.manual_seed(11)
+    m = nn.Sequential(nn.Linear(2048, 2048), nn.ReLU(), nn.Linear(2048, 2048), nn.ReLU(), nn.Linear(2048, 10)).eval()
+    cm, eng = engine(m, (2048,), tmp_path)
+    x = np.random.default_rng(3).standard_normal((5, 2048)).astype(np.float32)
+    got = run_dev(eng, x, 10)
+    assert eng.graph_kernels() == 1
+    assert np.allclose(got, oracle.run_model(m, x, "fused_ikj"), atol=ATOL, rtol=RTOL)
     eng.close()
     cm.close()
 
