@@ -424,7 +424,7 @@ static int layout_block(Model* m, ExecCtx* c, size_t min_bytes, bool* did_alloc)
       if ((st.kind == ST_GEMM && tc_gemm_supported(st.K, st.N)) || conv_tc_candidate(st)) any_tc = true;
   const size_t ks_floats = any_tc ? kKsplitWorkspaceFloats : 0;
   const size_t ks_b = round256(ks_floats * sizeof(float));
-  const size_t bar_b = 1024;  // chain-kernel barrier counters at 0, two-layer team counters at 256
+  const size_t bar_b = 16384;  // chain-kernel barrier counters at 0, two-layer team counters at 256
   const size_t need = std::max(arena + in_b + out_b + part_b + tick_b + ks_b + bar_b, min_bytes);
   bool fresh = false;
   if (!c->block || c->block_bytes < need) {
@@ -444,7 +444,7 @@ static int layout_block(Model* m, ExecCtx* c, size_t min_bytes, bool* did_alloc)
   c->ws_ksplit = ks_floats ? reinterpret_cast<float*>(c->block + arena + in_b + out_b + part_b + tick_b) : nullptr;
   c->chain_bar = reinterpret_cast<unsigned long long*>(c->block + arena + in_b + out_b + part_b + tick_b + ks_b);
   c->team_flags = reinterpret_cast<unsigned*>(reinterpret_cast<char*>(c->chain_bar) + 256);
-  static_assert(256 + kTcMlpTeamFlagWords * sizeof(unsigned) <= 1024, "team counters fit the counter area");
+  static_assert(256 + kTcMlpTeamFlagWords * sizeof(unsigned) <= 16384, "team counters fit the counter area");
   if (fresh && c->ws_tickets) {
     // tickets start at zero; every split-K launch leaves them at zero
     if (cudaMemset(c->ws_tickets, 0, tick_b) != cudaSuccess) {

@@ -144,17 +144,112 @@ struct TcMlpSmem {
   static constexpr int TOTAL = 1024 + STAGES * STAGE_BYTES + EPI_BYTES + HEAD_BYTES + BAR_BYTES;
 };
 
+// The small head over layer 2's columns [c0, c1) of this warp's rows, the
+// layer-2 epilogue applied per value on the way (head_chunk of tc_gemm.cuh):
+// partial sums of the head's outputs, in column order from zero.
+template <int HP4>
+__device__ __forceinline__ void mlp_head_part(float (&acc)[4 * HP4], const TcKernelParams& p2, const TcEpiSmem& e,
+                                              uint32_t base, int m, int c0, int c1) {
+#pragma unroll
+  for (int o = 0; o < 4 * HP4; ++o) acc[o] = 0.0f;
+#pragma unroll 1
+  for (int c = c0; c < c1; c += 32) {
+    uint32_t r[32];
+    __syncwarp();
+    FTB_TMEM_LD32(base + (uint32_t)c, r);
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+    const int cnt = min(32, c1 - c);
+    if (m < p2.M) {
+      if (cnt == 32)
+        head_chunk<HP4, true, false>(acc, r, p2, e, m, c, cnt);
+      else
+        head_chunk<HP4, false, false>(acc, r, p2, e, m, c, cnt);
+    }
+  }
+}
+
+// The head after layer 2 when a pair computes a single tile (and the launch
+// allows a different association of the head's sums than the sequential one
+// of two launches: by shape or pair 5): eight warps
+// share it -- the epilogue warps (grp 0) take layer 2's columns [0, 64), the
+// split warps (grp 1, idle once layer 1 is done) the rest -- and the epilogue
+// warps add the split warps' partial sums (staged in `part`, 128 rows x 16)
+// to theirs and store the outputs.  Every thread of both groups passes both
+// named barriers (id 3), also after an abort.
+template <int HP4>
+__device__ __forceinline__ void mlp_head_shared(const TcKernelParams& p2, const TcEpiSmem& e, uint32_t base, int m,
+                                                int row, int grp, bool ok, float* part) {
+  float acc[4 * HP4];
+  const int n2 = p2.N;
+  const int c0 = grp == 0 ? 0 : 64, c1 = grp == 0 ? min(64, n2) : n2;
+  asm volatile("bar.sync 3, 256;" ::: "memory");
+  if (ok && c0 < c1) {
+    mlp_head_part<HP4>(acc, p2, e, base, m, c0, c1);
+  } else {
+#pragma unroll
+    for (int o = 0; o < 4 * HP4; ++o) acc[o] = 0.0f;
+  }
+  if (grp == 1) {
+#pragma unroll
+    for (int o = 0; o < 4 * HP4; ++o) part[row * 16 + o] = acc[o];
+  }
+  asm volatile("bar.sync 3, 256;" ::: "memory");
+  if (grp == 0 && ok && m < p2.M) {
+#pragma unroll
+    for (int o = 0; o < 4 * HP4; ++o) {
+      if (o < e.hn) {
+        const float v = __fadd_rn(acc[o], part[row * 16 + o]);
+        p2.head.y[(int64_t)m * e.hn + o] = apply_epilogue(v, p2.head.epi, e.head_bb, nullptr, m, o, e.hn);
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ void mlp_head_dispatch(const TcKernelParams& p2, const TcEpiSmem& e, uint32_t base, int m,
+                                                  int row, int grp, bool ok, float* part) {
+  switch (e.hp) {
+    case 4: mlp_head_shared<1>(p2, e, base, m, row, grp, ok, part); break;
+    case 8: mlp_head_shared<2>(p2, e, base, m, row, grp, ok, part); break;
+    case 12: mlp_head_shared<3>(p2, e, base, m, row, grp, ok, part); break;
+    default: mlp_head_shared<4>(p2, e, base, m, row, grp, ok, part); break;
+  }
+}
+
 // Split of layer 1 over a team of pairs (S = 1: no split).
 struct TcMlpTeam {
   float* ws;         // helper sums: per tile and CTA rank 128 rows x 256 columns, as [chunk][group of 4][row] float4s
-  unsigned* flags;   // [2 tiles]: helper CTAs that published their sums, per tile and CTA rank
+  unsigned* flags;   // [tile][CTA rank][group of four chunks]: helper warps that published those sums
   unsigned* depart;  // CTAs that left the launch
   int S;
-  int pad;
+  int share_head;  // a pair with a single tile shares the head between its warp groups
 };
 
 constexpr int kTcMlpMaxTeam = 2;
-constexpr int kTcMlpTeamFlagWords = 160;  // 2 x tiles (<= 74) + the departure counter, rounded
+constexpr int kTcMlpMaxChunks = 8;  // 32-column chunks of h (N1 <= 256)
+constexpr int kTcMlpFlagStride = 32;  // counter words per (tile, CTA rank): one 128-byte line each
+
+// Bounded wait (one thread) until *f reaches `want`; on timeout it raises
+// this CTA's and the peer's abort flags and records error code 10.
+__device__ __forceinline__ int team_wait(const unsigned* f, unsigned want, volatile int* abort_flag,
+                                         uint32_t peer_abort, int* err) {
+  const uint64_t t0 = global_ns();
+  for (uint32_t it = 0;; ++it) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+    if (v >= want) return 1;
+    __nanosleep(64);
+    if ((it & 63u) == 63u) {
+      if (*abort_flag) return 0;
+      if (global_ns() - t0 > kTcWaitLimitNs) {
+        *abort_flag = 1;
+        st_cluster_u32(peer_abort, 1u);
+        atomicCAS(err, 0, 10);
+        return 0;
+      }
+    }
+  }
+}
+constexpr int kTcMlpTeamFlagWords = 2400;  // [tile][CTA rank] lines of chunk counters (2 x 37 x 32) + the departure counter
 
 // p1: layer 1 (M, K = K1, N = N1, bias, epi); p2: layer 2 (K = N1, N = N2,
 // bias, epi, output Y / head).  Roles as in the SM-pair kernel; the
@@ -189,7 +284,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
   uint64_t* never = drain + 1;          // never arrived on (stall_test)
   volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(never + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(never + 1) + 1;
-  volatile int* team_ok = reinterpret_cast<volatile int*>(never + 1) + 2;  // owner: the helpers' sums arrived
 
   const uint32_t rank = cluster_ctarank();
   const uint32_t peer = rank ^ 1u;
@@ -212,6 +306,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
   const int kb_hi = teamed ? ((member + 1) * nk1) / S : nk1;
   const int nkl = kb_hi - kb_lo;
   auto u_next = [&](int u) { return teamed ? tiles : u + npairs; };
+  // one tile for this pair and a head after layer 2: the split warps share
+  // the head (they are idle once layer 1 is done)
+  const bool head_shared = team.share_head && owner && p2.head.n > 0 && u_first < tiles && u_next(u_first) >= tiles;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -391,6 +488,25 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
         if (lane == 0) mbar_arrive_cluster(cluster_addr(&conv[s], 0));
       }
     }
+    if (head_shared) {
+      // the second half of layer 2's columns through the head
+      const int qq = warp & 3;
+      const int row = qq * 32 + lane;
+      const int m = u_first * 256 + (int)rank * kTcBM + row;
+      const bool okh = ok && pair_wait_warp(accf2, 0u, abort_flag, peer_abort, p1.err, 7);
+      tc_fence_after();
+      TcEpiSmem es;
+      es.tr = nullptr;
+      es.stage = nullptr;
+      es.head_w = head_smem;  // staged by the epilogue warps (tc_epi_setup) at the start
+      es.bias_a = head_smem + kTcMaxHeadK * kTcMaxHeadN;
+      es.head_bb = es.bias_a + kTcMaxHeadK;
+      es.hn = p2.head.n;
+      es.hp = (es.hn + 3) & ~3;
+      mlp_head_dispatch(p2, es, tmem + ACC2 + ((uint32_t)(qq * 32) << 16), m, row, 1, okh,
+                        reinterpret_cast<float*>(a_tile(0)));
+      tc_fence_before();
+    }
   } else {
     // warps 6..9: convert h, then layer 2's epilogue, for this CTA's 128 rows
     // (one TMEM lane quarter each)
@@ -423,7 +539,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
         // helper: publish this CTA's raw layer-1 sums, then count them in
         // layout [chunk][float4 group][row] of float4s: a warp's store is 512
         // contiguous bytes (its 32 rows' group i), and so is the owner's load
+        // (each warp counts its 32 rows of a chunk in as soon as they are stored)
         float4* dst = reinterpret_cast<float4*>(team.ws + (size_t)(u * 2 + (int)rank) * 128 * 256) + row;
+        unsigned* fl = team.flags + (2 * u + (int)rank) * kTcMlpFlagStride;
         for (int c = 0; c < nch; ++c) {
           __syncwarp();
           FTB_TMEM_LD32(tmem + lanes + (uint32_t)(32 * c), r);
@@ -432,50 +550,36 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
           for (int i = 0; i < 8; ++i)
             dst[(c * 8 + i) * 128] = make_float4(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1]),
                                                  __uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3]));
+          // each group of four chunks is published with one release (a
+          // release waits for the warp's stores: one per chunk would stall
+          // the loop an L2 round trip per chunk)
+          if ((c & 3) == 3 || c + 1 == nch) {
+            __syncwarp();
+            if (lane == 0) asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(fl + (c >> 2)) : "memory");
+          }
         }
         tc_fence_before();
-        asm volatile("bar.sync 1, 128;" ::: "memory");
-        if (threadIdx.x == 192) {
-          __threadfence();
-          atomicAdd(team.flags + 2 * u + (int)rank, 1u);
-        }
         continue;
-      }
-      if (teamed) {
-        // owner: the S - 1 helpers of this tile have published this CTA's rows
-        if (threadIdx.x == 192) {
-          int tok = 1;
-          const unsigned* f = team.flags + 2 * u + (int)rank;
-          const uint64_t t0 = global_ns();
-          for (uint32_t it2 = 0;; ++it2) {
-            unsigned v;
-            asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
-            if ((int)v >= S - 1) break;
-            if ((it2 & 63u) == 63u) {
-              if (*abort_flag) {
-                tok = 0;
-                break;
-              }
-              if (global_ns() - t0 > kTcWaitLimitNs) {
-                *abort_flag = 1;
-                st_cluster_u32(peer_abort, 1u);
-                atomicCAS(p1.err, 0, 10);
-                tok = 0;
-                break;
-              }
-            }
-            __nanosleep(32);
-          }
-          *team_ok = tok;
-        }
-        asm volatile("bar.sync 1, 128;" ::: "memory");
-        if (!(ok = *team_ok != 0)) break;
       }
       // the helper's sums of this thread's row (chunk c at 32 c), each chunk
       // loaded while the one before it is converted
       const float4* hrow = reinterpret_cast<const float4*>(team.ws + (size_t)(u * 2 + (int)rank) * 128 * 256) + row;
+      const unsigned* hfl = team.flags + (2 * u + (int)rank) * kTcMlpFlagStride;
+      // the helper's four warps have stored chunk c of this CTA's rows (they
+      // publish groups of four chunks; lane 0 waits, bounded; the warp then reads)
+      auto chunk_ready = [&](int c) -> bool {
+        if (c & 3) return true;  // published with the first chunk of its group of four
+        int okc = 1;
+        if (lane == 0) okc = team_wait(hfl + (c >> 2), 4u, abort_flag, peer_abort, p1.err);
+        okc = __shfl_sync(0xffffffffu, okc, 0);
+        __syncwarp();
+        return okc != 0;
+      };
       float4 pn[8];
-      if (teamed) mlp_load_partial(pn, hrow);
+      if (teamed) {
+        if (!(ok = chunk_ready(0))) break;
+        mlp_load_partial(pn, hrow);
+      }
       __syncwarp();
       FTB_TMEM_LD32(tmem + lanes, r);
       FTB_TMEM_WAIT_LD32(r);
@@ -484,7 +588,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
         uint32_t hi[32], lo[32];
         if (teamed) {
           mlp_add_partial(r, pn);
-          if (c + 1 < nch) mlp_load_partial(pn, hrow + (c + 1) * 8 * 128);
+          if (c + 1 < nch) {
+            if (!(ok = chunk_ready(c + 1))) break;
+            mlp_load_partial(pn, hrow + (c + 1) * 8 * 128);
+          }
         }
         const float* b = b1s + 32 * c;
         if (ep_bias && ep_relu) mlp_split_chunk<true, true>(r, b, hi, lo);
@@ -509,12 +616,23 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
       FTB_TMEM_WAIT_LD32(r);  // nothing left in flight if the loop gave up
       g += (uint32_t)nch;
       if (!ok) break;
+      if (head_shared) break;  // the head follows, shared with the split warps
       if (!(ok = pair_wait_warp(accf2, tc & 1u, abort_flag, peer_abort, p1.err, 7))) break;
       tc_fence_after();
       tc_epilogue_block<kTcMlpN2>(p2, &map_y, e, tmem + ACC2 + lanes, m0, 0, kTcMlpN2, q, lane, p2.epi, 0);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(cluster_addr(acce2, 0));
+    }
+    if (head_shared) {
+      // the first half of layer 2's columns through the head, plus the split
+      // warps' half, then the outputs
+      const int row = q * 32 + lane;
+      const int m = u_first * 256 + (int)rank * kTcBM + row;
+      const bool okh = ok && pair_wait_warp(accf2, 0u, abort_flag, peer_abort, p1.err, 7);
+      tc_fence_after();
+      mlp_head_dispatch(p2, e, tmem + ACC2 + lanes, m, row, 0, okh, reinterpret_cast<float*>(a_tile(0)));
+      tc_fence_before();
     }
     if (lane == 0) bulk_wait_all();
   }
@@ -525,13 +643,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
   }
-  if (teamed && threadIdx.x == 0) {
-    // every role of this CTA is done: count it out; the last CTA resets the counters
-    __threadfence();
-    const unsigned d = atomicAdd(team.depart, 1u);
-    if (d == gridDim.x - 1) {
-      for (int i = 0; i < 2 * tiles; ++i) atomicExch(team.flags + i, 0u);
-      atomicExch(team.depart, 0u);
+  if (teamed) {
+    // every role of this CTA is done: count it out; the last CTA out resets
+    // the chunk counters (all threads, plain stores: the next launch sees
+    // them once this one has completed)
+    volatile int* last = reinterpret_cast<volatile int*>(never + 1) + 2;
+    if (threadIdx.x == 0) {
+      __threadfence();
+      *last = atomicAdd(team.depart, 1u) == gridDim.x - 1;
+    }
+    __syncthreads();
+    if (*last) {
+      for (int i = threadIdx.x; i < 2 * tiles * 2; i += blockDim.x) team.flags[(i >> 1) * kTcMlpFlagStride + (i & 1)] = 0u;
+      if (threadIdx.x == 0) *team.depart = 0u;
     }
   }
 }
@@ -629,9 +753,12 @@ inline int launch_tc_mlp(const TcArgs& t1, const TcWeights& w1, const TcArgs& t2
   std::memset(&team, 0, sizeof(team));
   team.S = 1;
   if (team_flags && t1.ws) {
+    // by shape or asked for (pair 5): the sums may be associated differently
+    // from two launches -- layer 1 split over teams, the head shared
+    team.share_head = 1;
     const int S = tc_mlp_team_size(tiles, (int)((t1.K + 15) / 16), max_pairs);
     const size_t need = (size_t)(S - 1) * (size_t)tiles * 2 * 128 * 256;
-    if (S > 1 && need <= t1.ws_floats && 2 * tiles <= kTcMlpTeamFlagWords - 1) {
+    if (S > 1 && need <= t1.ws_floats && 2 * tiles * kTcMlpFlagStride <= kTcMlpTeamFlagWords - 1) {
       team.S = S;
       team.ws = t1.ws;
       team.flags = team_flags;

@@ -131,7 +131,8 @@ FORGETUNE_EXPORT int ftb_model_set_policy(void* model, int policy);
  * pair qualifies: `mlp_step` in ftb_describe_blob's output; else as 0),
  * 5 = the same, with this step's k-blocks split over a team of two pairs per
  * tile when the tiles leave a second pair each free (the helper's sums are
- * added to the owner's);
+ * added to the owner's), and, where a pair computes a single tile, the head
+ * shared by two warp groups (each sums half of the columns);
  * 0 = chosen by shape (may pick split-K, or the two-layer launch, split over
  * teams when the tiles are few, when neither step carries a configuration).
  * fuse_head: compute a following small-N head in the epilogue.
