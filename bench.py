@@ -563,6 +563,8 @@ def run_ours(args) -> int:
                "h2d_bytes_per_step": G * IN_F * 4, "d2h_bytes_per_step": G * OUT_F * 4,
                "h2d_bytes_per_step_per_gpu": B * IN_F * 4, "d2h_bytes_per_step_per_gpu": int(out_host.nbytes),
                "ms_per_step": 1000.0 * e2e_s / args.steps}
+        e2e.update(host_link(xh, dev, stream, max_over_ranks, e2e["ms_per_step"]))
+        del xh
 
         # wide MLP at box scale: 262144 rows split over the GPUs, generated per shard on the device
         extras["wide_mlp"] = wide_mlp_extra(world, rank, dev, stream, timer, tc_peak, max_over_ranks, barrier)
@@ -599,6 +601,30 @@ def run_ours(args) -> int:
     if world > 1:
         dist.destroy_process_group()
     return 0
+
+
+def host_link(xh, dev, stream, max_over_ranks, e2e_ms: float) -> dict:
+    """The host link's own speed for this step's input: one pinned-host ->
+    device copy of the same bytes (cudaMemcpyAsync), timed with CUDA events
+    over five copies after one warm-up, slowest rank.  The e2e step cannot
+    beat it (the run path overlaps the output's copy and the compute with
+    it), so link_bound_ms / e2e ms_per_step is e2e's fraction of the link."""
+    import torch
+    d = torch.empty(xh.shape, dtype=xh.dtype, device=dev)
+    reps = 5
+    with torch.cuda.stream(stream):
+        d.copy_(xh, non_blocking=True)
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        for _ in range(reps):
+            d.copy_(xh, non_blocking=True)
+        t1.record(stream)
+    t1.synchronize()
+    ms = max_over_ranks(t0.elapsed_time(t1) / reps)
+    del d
+    nbytes = xh.numel() * xh.element_size()
+    return {"link_h2d_gbs": nbytes / (ms / 1000.0) / 1e9, "link_bound_ms": ms, "frac_of_link": ms / e2e_ms,
+            "link_basis": "pinned host -> device copy of this step's input bytes, CUDA events, slowest rank"}
 
 
 def sweep_extra(cm, eng, dev, stream, timer, tc_peak) -> dict:

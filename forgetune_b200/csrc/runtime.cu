@@ -1007,6 +1007,10 @@ static int resolve_devices(Model* m, std::vector<int>* devs) {
 // host-to-host runs whose input and output each fit this many bytes go
 // through pinned staging with the copies inside the graph
 static constexpr size_t kHostStageBytes = 256u << 10;
+// Every CTA of the chain kernel reads all input rows: read straight from
+// mapped host memory only while that stays a few PCIe round trips (one
+// row of the tiny MLP on 32 CTAs is 100 KB), else copy them in first.
+static constexpr size_t kZeroCopyReadBytes = 128u << 10;
 
 // rows per pipeline chunk so one chunk's input is about 32 MiB
 static int64_t chunk_rows_for(const Program& p, int64_t batch) {
@@ -1051,7 +1055,7 @@ static int run_host_one(Model* m, int dev, const float* in, float* out, int64_t 
         }
       }
       std::memcpy(c->h_in, in, in_b);
-      if (chain_takes(m, rep, batch)) {
+      if (chain_takes(m, rep, batch) && in_b * (size_t)rep->chain_grid <= kZeroCopyReadBytes) {
         // the one-launch chain reads its input rows from and writes its
         // output to the mapped staging buffers itself: no copy at all
         rc = run_graph(m, rep, c, c->h_in_dev, c->h_out_dev, batch, c->stream);

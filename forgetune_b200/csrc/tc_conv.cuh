@@ -247,7 +247,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           hi[j] = tf32_rna(c[j]);
-          lo[j] = tf32_rna(c[j] - hi[j]);
+          lo[j] = tf32_rna_rem(c[j] - hi[j]);
         }
         const int s = (int)(it % STAGES);
         if (!(ok = mbar_wait_warp(&full[s], (it / STAGES) & 1u, abort_flag, p.err, 6))) break;

@@ -321,6 +321,18 @@ __device__ __forceinline__ float tf32_rna(float v) {
   return __uint_as_float(r);
 }
 
+// The low part of a 3xTF32 split, rem = v - tf32_rna(v), rounded the same
+// way (to nearest, ties away from zero) with integer operations on its bit
+// pattern: half the weight of the 13 dropped mantissa bits is added to the
+// magnitude and the bits are cleared, a carry moving into the exponent as
+// rounding does.  For every finite rem this gives the bits of cvt.rna.tf32;
+// it runs on the integer pipe, so a split costs one conversion per value on
+// the quarter-rate conversion pipe instead of two.  rem is finite whenever
+// v is; for v = +-Inf (rem NaN) the result is a zero.
+__device__ __forceinline__ float tf32_rna_rem(float rem) {
+  return __uint_as_float((__float_as_uint(rem) + 0x1000u) & 0xFFFFE000u);
+}
+
 #define FTB_TMEM_LD32(taddr, r)                                                                              \
   asm volatile(                                                                                              \
       "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17," \
@@ -345,10 +357,10 @@ __device__ __forceinline__ void tc_split_a(float4* hi, float4* lo, int t128) {
     h.y = tf32_rna(v.y);
     h.z = tf32_rna(v.z);
     h.w = tf32_rna(v.w);
-    l.x = tf32_rna(v.x - h.x);
-    l.y = tf32_rna(v.y - h.y);
-    l.z = tf32_rna(v.z - h.z);
-    l.w = tf32_rna(v.w - h.w);
+    l.x = tf32_rna_rem(v.x - h.x);
+    l.y = tf32_rna_rem(v.y - h.y);
+    l.z = tf32_rna_rem(v.z - h.z);
+    l.w = tf32_rna_rem(v.w - h.w);
     hi[idx] = h;
     lo[idx] = l;
   }

@@ -24,7 +24,10 @@
 // share one launch.
 //
 // Few tiles (a tile count that leaves at least one idle pair per tile): a
-// team of S = 2 pairs computes one tile.  Member s runs layer 1 over its own
+// team of S = 2 pairs computes one tile.  Many tiles whose last round would
+// leave at least half of the pairs idle: the full rounds run unsplit and the
+// tiles of the last round by teams (team.split_from = the first of them), so
+// that round takes half of a tile's layer 1 instead of all of it.  Member s runs layer 1 over its own
 // contiguous half of the k-blocks only; the helper (s = 1) writes its raw
 // layer-1 sums (this CTA's 128 rows x 256 columns) to a workspace and bumps
 // the tile's per-CTA counter; the owner (s = 0) waits for it (bounded), adds
@@ -105,7 +108,7 @@ __device__ __forceinline__ void mlp_split_chunk(const uint32_t (&r)[32], const f
       if (RELU) v = relu_keep_nan(v);
       const float h = tf32_rna(v);
       hi[4 * i + k] = __float_as_uint(h);
-      lo[4 * i + k] = __float_as_uint(tf32_rna(v - h));
+      lo[4 * i + k] = __float_as_uint(tf32_rna_rem(v - h));
     }
   }
 }
@@ -222,6 +225,7 @@ struct TcMlpTeam {
   unsigned* depart;  // CTAs that left the launch
   int S;
   int share_head;  // a pair with a single tile shares the head between its warp groups
+  int split_from;  // the first tile computed by a team (0: all of them)
 };
 
 constexpr int kTcMlpMaxTeam = 2;
@@ -295,20 +299,28 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
   const int nch = (p1.N + 31) / 32;  // chunks of h converted per tile
   const int pair = (int)cluster_index();
   const int npairs = (int)cluster_count();
-  // this pair's tiles and layer-1 k-blocks: all of them, or in a team one
-  // tile and the member's contiguous share of the k-blocks
+  // this pair's tiles: p, p + npairs, ... below split_from with all of layer
+  // 1's k-blocks; the tiles from split_from on (all of them when they are
+  // few, the last round when they are many) are shared by teams of S pairs:
+  // pair p < S x Lt is member p / Lt of tile split_from + p % Lt, with the
+  // member's contiguous share of the k-blocks; member 0 (the owner) also runs
+  // layer 2 and the head
   const int S = team.S;
-  const bool teamed = S > 1;
-  const int u_first = teamed ? pair % tiles : pair;
-  const int member = teamed ? pair / tiles : 0;
-  const bool owner = member == 0;
-  const int kb_lo = teamed ? (member * nk1) / S : 0;
-  const int kb_hi = teamed ? ((member + 1) * nk1) / S : nk1;
-  const int nkl = kb_hi - kb_lo;
-  auto u_next = [&](int u) { return teamed ? tiles : u + npairs; };
+  const bool teamed = S > 1;  // the launch splits some tiles
+  const int split_from = teamed ? team.split_from : tiles;
+  const int Lt = tiles - split_from;  // tiles computed by teams
+  const int team_u = (teamed && Lt > 0 && pair < S * Lt) ? split_from + pair % Lt : tiles;
+  const int member = (teamed && Lt > 0) ? pair / Lt : 0;
+  const int u_first = pair < split_from ? pair : team_u;
+  auto u_next = [&](int u) { return u + npairs < split_from ? u + npairs : (u < split_from ? team_u : tiles); };
+  auto in_team = [&](int u) { return u >= split_from; };
+  auto owner_of = [&](int u) { return !in_team(u) || member == 0; };
+  auto kb_lo_of = [&](int u) { return in_team(u) ? (member * nk1) / S : 0; };
+  auto kb_hi_of = [&](int u) { return in_team(u) ? ((member + 1) * nk1) / S : nk1; };
   // one tile for this pair and a head after layer 2: the split warps share
   // the head (they are idle once layer 1 is done)
-  const bool head_shared = team.share_head && owner && p2.head.n > 0 && u_first < tiles && u_next(u_first) >= tiles;
+  const bool head_shared =
+      team.share_head && u_first < tiles && owner_of(u_first) && p2.head.n > 0 && u_next(u_first) >= tiles;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -351,7 +363,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
     bool ok = true;
     for (int u = u_first; u < tiles && ok; u = u_next(u)) {
       const int m0 = u * 256 + (int)rank * kTcBM;
-      for (int kb = kb_lo; kb < kb_hi; ++kb, ++it) {
+      const int kb_hi = kb_hi_of(u);
+      for (int kb = kb_lo_of(u); kb < kb_hi; ++kb, ++it) {
         const int s = (int)(it % STAGES);
         if (!(ok = pair_wait_warp(&empty[s], ((it / STAGES) & 1u) ^ 1u, abort_flag, peer_abort, p1.err, 1))) break;
         if (elect_one()) {
@@ -362,7 +375,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
         }
         __syncwarp();
       }
-      for (int j = 0; j < nk2 && ok && owner; ++j, ++it) {
+      for (int j = 0; j < nk2 && ok && owner_of(u); ++j, ++it) {
         const int s = (int)(it % STAGES);
         if (!(ok = pair_wait_warp(&empty[s], ((it / STAGES) & 1u) ^ 1u, abort_flag, peer_abort, p1.err, 1))) break;
         if (elect_one()) {
@@ -382,6 +395,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
       for (int u = u_first; u < tiles && ok; u = u_next(u), ++tc) {
         // layer 1 into columns [0, 256); this tile's layer 2 of the previous
         // tile, issued earlier, has read its A there first
+        const int kb_lo = kb_lo_of(u), kb_hi = kb_hi_of(u);
         for (int kb = kb_lo; kb < kb_hi; ++kb, ++it) {
           const int s = (int)(it % STAGES);
           if (!(ok = pair_wait_warp(&conv[s], (it / STAGES) & 1u, abort_flag, peer_abort, p1.err, 4))) break;
@@ -413,7 +427,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
           }
           __syncwarp();
         }
-        if (!owner) continue;  // a helper's part ends with its layer-1 sums
+        if (!owner_of(u)) continue;  // a helper's part ends with its layer-1 sums
         // layer 2 into columns [256, 384), once the previous tile's epilogue drained them
         if (!(ok = pair_wait_warp(acce2, (tc & 1u) ^ 1u, abort_flag, peer_abort, p1.err, 2))) break;
         tc_fence_after();
@@ -476,7 +490,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
     uint32_t it = 0;
     bool ok = true;
     for (int u = u_first; u < tiles && ok; u = u_next(u)) {
-      for (int kb = 0; kb < nkl + (owner ? nk2 : 0); ++kb, ++it) {
+      const int nkl = kb_hi_of(u) - kb_lo_of(u);
+      for (int kb = 0; kb < nkl + (owner_of(u) ? nk2 : 0); ++kb, ++it) {
         const int s = (int)(it % STAGES);
         if (!(ok = pair_wait_warp(&full[s], (it / STAGES) & 1u, abort_flag, peer_abort, p1.err, 6))) break;
         if (kb < nkl) {
@@ -535,13 +550,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
       // chunk c+1 is loaded from TMEM while chunk c's stores complete
       uint32_t r[32];
       const int row = q * 32 + lane;  // this thread's row of the CTA's 128
-      if (!owner) {
+      if (!owner_of(u)) {
         // helper: publish this CTA's raw layer-1 sums, then count them in
         // layout [chunk][float4 group][row] of float4s: a warp's store is 512
         // contiguous bytes (its 32 rows' group i), and so is the owner's load
         // (each warp counts its 32 rows of a chunk in as soon as they are stored)
-        float4* dst = reinterpret_cast<float4*>(team.ws + (size_t)(u * 2 + (int)rank) * 128 * 256) + row;
-        unsigned* fl = team.flags + (2 * u + (int)rank) * kTcMlpFlagStride;
+        const int tu = u - split_from;  // this tile among the team tiles
+        float4* dst = reinterpret_cast<float4*>(team.ws + (size_t)(tu * 2 + (int)rank) * 128 * 256) + row;
+        unsigned* fl = team.flags + (2 * tu + (int)rank) * kTcMlpFlagStride;
         for (int c = 0; c < nch; ++c) {
           __syncwarp();
           FTB_TMEM_LD32(tmem + lanes + (uint32_t)(32 * c), r);
@@ -563,8 +579,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
       }
       // the helper's sums of this thread's row (chunk c at 32 c), each chunk
       // loaded while the one before it is converted
-      const float4* hrow = reinterpret_cast<const float4*>(team.ws + (size_t)(u * 2 + (int)rank) * 128 * 256) + row;
-      const unsigned* hfl = team.flags + (2 * u + (int)rank) * kTcMlpFlagStride;
+      const bool tsum = in_team(u);  // the helper's sums are added to this tile's
+      const int tu = tsum ? u - split_from : 0;
+      const float4* hrow = reinterpret_cast<const float4*>(team.ws + (size_t)(tu * 2 + (int)rank) * 128 * 256) + row;
+      const unsigned* hfl = team.flags + (2 * tu + (int)rank) * kTcMlpFlagStride;
       // the helper's four warps have stored chunk c of this CTA's rows (they
       // publish groups of four chunks; lane 0 waits, bounded; the warp then reads)
       auto chunk_ready = [&](int c) -> bool {
@@ -576,7 +594,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
         return okc != 0;
       };
       float4 pn[8];
-      if (teamed) {
+      if (tsum) {
         if (!(ok = chunk_ready(0))) break;
         mlp_load_partial(pn, hrow);
       }
@@ -586,7 +604,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
       for (int c = 0; c < nch; ++c) {
         const uint32_t gc = g + (uint32_t)c, qs = gc & 3u, use = gc >> 2;
         uint32_t hi[32], lo[32];
-        if (teamed) {
+        if (tsum) {
           mlp_add_partial(r, pn);
           if (c + 1 < nch) {
             if (!(ok = chunk_ready(c + 1))) break;
@@ -654,7 +672,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
     }
     __syncthreads();
     if (*last) {
-      for (int i = threadIdx.x; i < 2 * tiles * 2; i += blockDim.x) team.flags[(i >> 1) * kTcMlpFlagStride + (i & 1)] = 0u;
+      for (int i = threadIdx.x; i < 2 * Lt * 2; i += blockDim.x) team.flags[(i >> 1) * kTcMlpFlagStride + (i & 1)] = 0u;
       if (threadIdx.x == 0) *team.depart = 0u;
     }
   }
@@ -756,14 +774,28 @@ inline int launch_tc_mlp(const TcArgs& t1, const TcWeights& w1, const TcArgs& t2
     // by shape or asked for (pair 5): the sums may be associated differently
     // from two launches -- layer 1 split over teams, the head shared
     team.share_head = 1;
-    const int S = tc_mlp_team_size(tiles, (int)((t1.K + 15) / 16), max_pairs);
-    const size_t need = (size_t)(S - 1) * (size_t)tiles * 2 * 128 * 256;
-    if (S > 1 && need <= t1.ws_floats && 2 * tiles * kTcMlpFlagStride <= kTcMlpTeamFlagWords - 1) {
+    const int nk1 = (int)((t1.K + 15) / 16);
+    int S = tc_mlp_team_size(tiles, nk1, max_pairs);
+    int64_t split_from = 0, team_tiles = tiles;
+    if (S == 1 && tiles > max_pairs) {
+      // many tiles: the full rounds unsplit, a last round that leaves at
+      // least half of the pairs idle split over teams
+      const int64_t full = tiles / max_pairs * max_pairs;
+      const int S_last = tc_mlp_team_size(tiles - full, nk1, max_pairs);
+      if (tiles > full && S_last > 1) {
+        S = S_last;
+        split_from = full;
+        team_tiles = tiles - full;
+      }
+    }
+    const size_t need = (size_t)(S - 1) * (size_t)team_tiles * 2 * 128 * 256;
+    if (S > 1 && need <= t1.ws_floats && 2 * team_tiles * kTcMlpFlagStride <= kTcMlpTeamFlagWords - 1) {
       team.S = S;
+      team.split_from = (int)split_from;
       team.ws = t1.ws;
       team.flags = team_flags;
       team.depart = team_flags + kTcMlpTeamFlagWords - 1;
-      pairs = (unsigned)(tiles * S);
+      pairs = split_from > 0 ? (unsigned)max_pairs : (unsigned)(tiles * S);
     }
   }
   // W1^T halves of 128 rows, W2^T halves of 64 rows, k-blocks of 16

@@ -53,17 +53,18 @@ def test_tensor_core_wait_timeout_is_reported_and_recoverable(pair, tmp_path):
     cm.close()
 
 
-@pytest.mark.parametrize("pair,rows", [(4, 3000), (5, 2048)])
+@pytest.mark.parametrize("pair,rows", [(4, 3000), (5, 2048), (5, 20000)])
 def test_two_layer_kernel_wait_timeout_is_reported_and_recoverable(pair, rows, tmp_path):
     """The two-layer kernel (both layers and the head in one launch, the
     hidden layer in tensor memory), unsplit and split over teams of pairs:
     its MMA thread's wait runs out, every role of both CTAs leaves through
-    its own bounded waits (a team owner also stops waiting for its helpers),
+    its own bounded waits (a team owner also stops waiting for its helpers;
+    at 20000 rows the full rounds run unsplit and the last round by teams),
     the run returns -5, and the same context then computes correctly again."""
     torch.manual_seed(4)
     m = nn.Sequential(nn.Linear(256, 256), nn.ReLU(), nn.Linear(256, 128), nn.ReLU(), nn.Linear(128, 10)).eval()
     cm = compile_model(m, (torch.randn(2, 256),), output_dir=str(tmp_path), autotune=False, enable_fusion=True,
-                       kernel_variant="fused_ikj", dynamic_batch=True, max_batch_size=4096,
+                       kernel_variant="fused_ikj", dynamic_batch=True, max_batch_size=20000,
                        gpu_kernel="tcgen05", verify=False)
     with open(cm.manifest()["artifacts"]["graph_blob"], "rb") as f:
         eng = _native.EngineModel(f.read())
