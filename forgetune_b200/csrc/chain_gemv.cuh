@@ -26,7 +26,19 @@
 // of the k terms differs from the per-layer kernels: results agree within
 // the tolerance, not bit for bit.
 //
-// The grid barrier is a 64-bit arrival counter in the context's workspace:
+// Tagged hand-over (up to 8 rows, when the context has a tag area; at 16
+// rows the barrier form measured faster, 20.5 vs 22.3 us for the tiny MLP):
+// a layer whose output a
+// later layer reads also stores each value as one 64-bit word, the value's
+// bits with the launch's tag above them; a reader polls its words (bounded)
+// until they carry this launch's tag.  A word is written and read whole, so
+// it needs no fence and no barrier: a CTA starts the next layer as soon as
+// the values it reads have arrived.  The tag is 0x80000000 | (epoch & 0x7fffffff)
+// for a per-context launch counter that the last CTA out advances, so words
+// of earlier launches (or of a launch that gave up) never match.
+//
+// The grid barrier (without a tag area) is a 64-bit arrival counter in the
+// context's workspace:
 // barrier b of a launch completes when the counter reaches (b + 1) x grid.
 // Every CTA increments a second counter as it leaves; the last one resets
 // both to zero, so each launch starts from zero, also after a wait that gave
@@ -46,6 +58,7 @@ namespace ftb {
 
 constexpr int kChainMaxLayers = 24;
 constexpr int kChainMaxRows = 16;
+constexpr int kChainTagRows = 8;  // the tagged hand-over up to this many rows, grid barriers above
 constexpr int kChainWarps = 8;
 constexpr int kChainSmemBytes = 220 * 1024;  // input rows (M x K floats) and cached weight rows
 constexpr unsigned long long kChainWaitNs = 2000000000ull;
@@ -58,13 +71,16 @@ struct ChainLayer {
   float* y;           // [M, N]
   int K, N;
   uint32_t epi;       // EPI_* flags; a bias is added after the k sum
-  int pad;
+  int tag_off;        // this layer's tagged output in ChainParams::tags (words), or -1 (not read by a later layer)
+  int a_src;          // the layer whose output `a` is (tagged reads), or -1
+  int res_src;        // the layer whose output `res` is (tagged reads), or -1
 };
 
 struct ChainParams {
   int n_layers;
   int M;
-  unsigned long long* bar;  // [0] arrivals, [1] departures; zero between launches
+  unsigned long long* bar;  // [0] arrivals, [1] departures (zero between launches), [3] launch counter
+  unsigned long long* tags; // tag area (tagged hand-over), or null (grid barriers)
   int* err;                 // the replica's error word (mapped host memory)
   int stall_test;           // failure-detection hook: CTA 0 never arrives at the first barrier
   int xs_floats;            // shared memory for the input rows (floats, a multiple of 4)
@@ -106,6 +122,34 @@ __device__ __forceinline__ bool chain_grid_sync(unsigned long long* bar, int* er
   return *ok_smem != 0;
 }
 
+__device__ __forceinline__ unsigned long long chain_ld_word(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void chain_st_word(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+// The value of a tagged word once it carries `tag` (polled, bounded); false
+// when the wait gave up (error code 20 + b recorded) or `*abort` was raised.
+__device__ __forceinline__ bool chain_wait_word(const unsigned long long* p, unsigned long long& w, uint32_t tag,
+                                                int* err, int b, volatile int* abort) {
+  if ((uint32_t)(w >> 32) == tag) return true;
+  const unsigned long long t0 = chain_now();
+  for (uint32_t it = 0;; ++it) {
+    w = chain_ld_word(p);
+    if ((uint32_t)(w >> 32) == tag) return true;
+    if ((it & 15u) == 15u) {
+      if (*abort) return false;
+      if (chain_now() - t0 > kChainWaitNs) {
+        atomicCAS(err, 0, 20 + b);
+        *abort = 1;
+        return false;
+      }
+    }
+  }
+}
+
 __device__ __forceinline__ void chain_cp_async16(void* dst, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
                : "memory");
@@ -132,13 +176,19 @@ __global__ void __launch_bounds__(kChainWarps * 32, 1) chain_gemv_kernel(const _
   extern __shared__ float4 chain_smem[];
   float4* chain_xs = chain_smem;  // [M][K/4] of the current layer
   __shared__ int ok_smem;
+  __shared__ int abort_smem;  // a tagged wait of this CTA gave up
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int gw = blockIdx.x * kChainWarps + warp;
   const int nw = gridDim.x * kChainWarps;
   const int M = p.M, NL = p.n_layers;
   const bool cached = p.wcache_per_warp > 0;
   float* wcache = reinterpret_cast<float*>(chain_smem) + p.xs_floats + (size_t)warp * p.wcache_per_warp;
-  bool ok = !(p.stall_test && blockIdx.x == 0);  // the hook: CTA 0 leaves without arriving
+  bool ok = !(p.stall_test && blockIdx.x == 0);  // the hook: CTA 0 leaves without arriving (or writing)
+  const bool tagged = p.tags != nullptr;
+  // this launch's tag (the counter advances when the previous launch's last CTA left)
+  const unsigned long long epoch = tagged ? *reinterpret_cast<volatile unsigned long long*>(p.bar + 3) + 1 : 0;
+  const uint32_t tag = 0x80000000u | ((uint32_t)epoch & 0x7fffffffu);
+  if (threadIdx.x == 0) abort_smem = 0;
   // This warp's weight rows of every layer: copied into shared memory now
   // (one cp.async group per layer, layer 0's first), or, when they do not
   // fit, prefetched into L2.  They do not depend on the activations, so a
@@ -173,7 +223,29 @@ __global__ void __launch_bounds__(kChainWarps * 32, 1) chain_gemv_kernel(const _
       // one per row (2 us less per forward of the tiny MLP at 2..16 rows)
       constexpr int SR = 4;
       const int total = M * K4;
-      if (total <= (int)blockDim.x) {
+      if (tagged && L.a_src >= 0) {
+        // from the producing layer's tagged words, as they arrive: up to
+        // four words per thread loaded before the first wait
+        const unsigned long long* src = p.tags + p.layer[L.a_src].tag_off;
+        float* xs = reinterpret_cast<float*>(chain_xs);
+        const int words = M * L.K;
+        for (int i0 = threadIdx.x; i0 < words && ok; i0 += SR * blockDim.x) {
+          unsigned long long t[SR];
+#pragma unroll
+          for (int r = 0; r < SR; ++r) {
+            const int i = i0 + r * blockDim.x;
+            t[r] = i < words ? chain_ld_word(src + i) : 0ull;
+          }
+#pragma unroll
+          for (int r = 0; r < SR; ++r) {
+            const int i = i0 + r * blockDim.x;
+            if (i < words && ok) {
+              ok = chain_wait_word(src + i, t[r], tag, p.err, l - 1, &abort_smem);
+              xs[i] = __uint_as_float((uint32_t)t[r]);
+            }
+          }
+        }
+      } else if (total <= (int)blockDim.x) {
         if ((int)threadIdx.x < total) chain_xs[threadIdx.x] = __ldcg(a4 + threadIdx.x);
       } else {
         for (int i0 = threadIdx.x; i0 < total; i0 += SR * blockDim.x) {
@@ -193,6 +265,7 @@ __global__ void __launch_bounds__(kChainWarps * 32, 1) chain_gemv_kernel(const _
     }
     if (cached) chain_cp_wait(NL - 1 - l);  // this thread's copies of this layer's rows have landed
     __syncthreads();                         // (and every other thread's, and the input rows)
+    if (tagged && abort_smem) break;         // a wait of this CTA gave up: leave
     int j = 0;
     for (int n = gw; n < N; n += nw, ++j) {
       const float4* w4 = cached ? reinterpret_cast<const float4*>(wcache + woff + j * L.K)
@@ -200,7 +273,18 @@ __global__ void __launch_bounds__(kChainWarps * 32, 1) chain_gemv_kernel(const _
       // the epilogue's operands are loaded with the weights, not after the sums
       const int64_t mrow = lane < M ? lane : 0;
       const float bv = L.bias ? ((L.epi & EPI_BIAS_ROWS) ? __ldg(L.bias + mrow * N + n) : __ldg(L.bias + n)) : 0.0f;
-      const float rv = (L.epi & EPI_RESIDUAL) ? __ldcg(L.res + mrow * N + n) : 0.0f;
+      float rv = 0.0f;
+      if (L.epi & EPI_RESIDUAL) {
+        if (tagged && L.res_src >= 0) {
+          // an earlier layer's output, from its tagged words
+          const unsigned long long* rp = p.tags + p.layer[L.res_src].tag_off + mrow * N + n;
+          unsigned long long w = chain_ld_word(rp);
+          if (lane < M && !chain_wait_word(rp, w, tag, p.err, l - 1, &abort_smem)) w = 0ull;
+          rv = __uint_as_float((uint32_t)w);
+        } else {
+          rv = __ldcg(L.res + mrow * N + n);
+        }
+      }
       float acc[MB];
 #pragma unroll
       for (int m = 0; m < MB; ++m) acc[m] = 0.0f;
@@ -249,10 +333,14 @@ __global__ void __launch_bounds__(kChainWarps * 32, 1) chain_gemv_kernel(const _
         if (L.epi & EPI_RESIDUAL) v = __fadd_rn(v, rv);
         if (L.epi & EPI_RELU_POST) v = relu_keep_nan(v);
         L.y[mrow * N + n] = v;
+        if (tagged && L.tag_off >= 0)
+          chain_st_word(p.tags + L.tag_off + mrow * N + n, ((unsigned long long)tag << 32) | __float_as_uint(v));
       }
     }
     woff += j * L.K;
-    if (l + 1 < NL) {
+    if (l + 1 < NL && tagged) {
+      __syncthreads();  // every warp is done with this layer's input rows before the next ones land
+    } else if (l + 1 < NL) {
       if (!cached) {
         // the next layer's weight rows of this warp into L1 while the barrier waits
         const ChainLayer& Ln = p.layer[l + 1];
@@ -275,6 +363,7 @@ __global__ void __launch_bounds__(kChainWarps * 32, 1) chain_gemv_kernel(const _
     if (d == gridDim.x - 1) {
       atomicExch(p.bar, 0ull);
       atomicExch(p.bar + 1, 0ull);
+      if (tagged) atomicExch(p.bar + 3, epoch);  // the next launch tags with epoch + 1
     }
   }
 }

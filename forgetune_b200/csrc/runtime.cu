@@ -121,6 +121,10 @@ struct ExecCtx {
   // grid-barrier counters of the chain kernel and the two-layer kernel's
   // team counters (zero between launches)
   unsigned long long* chain_bar = nullptr;
+  // the chain kernel's tagged hand-over words (kChainTagRows rows x the sum of the
+  // layers' widths), or null when the launch list is not a chain of GEMMs
+  unsigned long long* chain_tags = nullptr;
+  size_t chain_tag_words = 0;
   unsigned* team_flags = nullptr;
   bool in_use = false;
   // pinned host staging for small host-to-host runs (allocated on first use):
@@ -425,7 +429,19 @@ static int layout_block(Model* m, ExecCtx* c, size_t min_bytes, bool* did_alloc)
   const size_t ks_floats = any_tc ? kKsplitWorkspaceFloats : 0;
   const size_t ks_b = round256(ks_floats * sizeof(float));
   const size_t bar_b = 16384;  // chain-kernel barrier counters at 0, two-layer team counters at 256
-  const size_t need = std::max(arena + in_b + out_b + part_b + tick_b + ks_b + bar_b, min_bytes);
+  // chain-kernel tag words: kChainTagRows rows of every layer's output
+  size_t tag_words = 0;
+  {
+    bool chain = !p.steps.empty() && p.steps.size() <= (size_t)kChainMaxLayers;
+    int64_t sum_n = 0;
+    for (const Step& st : p.steps) {
+      chain = chain && st.kind == ST_GEMM;
+      sum_n += st.N;
+    }
+    if (chain) tag_words = (size_t)kChainTagRows * (size_t)sum_n;
+  }
+  const size_t tag_b = round256(tag_words * sizeof(unsigned long long));
+  const size_t need = std::max(arena + in_b + out_b + part_b + tick_b + ks_b + bar_b + tag_b, min_bytes);
   bool fresh = false;
   if (!c->block || c->block_bytes < need) {
     int rc = alloc_block(c, need);
@@ -444,6 +460,9 @@ static int layout_block(Model* m, ExecCtx* c, size_t min_bytes, bool* did_alloc)
   c->ws_ksplit = ks_floats ? reinterpret_cast<float*>(c->block + arena + in_b + out_b + part_b + tick_b) : nullptr;
   c->chain_bar = reinterpret_cast<unsigned long long*>(c->block + arena + in_b + out_b + part_b + tick_b + ks_b);
   c->team_flags = reinterpret_cast<unsigned*>(reinterpret_cast<char*>(c->chain_bar) + 256);
+  c->chain_tag_words = tag_words;
+  c->chain_tags = tag_words ? reinterpret_cast<unsigned long long*>(reinterpret_cast<char*>(c->chain_bar) + bar_b)
+                            : nullptr;
   static_assert(256 + kTcMlpTeamFlagWords * sizeof(unsigned) <= 16384, "team counters fit the counter area");
   if (fresh && c->ws_tickets) {
     // tickets start at zero; every split-K launch leaves them at zero
@@ -454,8 +473,10 @@ static int layout_block(Model* m, ExecCtx* c, size_t min_bytes, bool* did_alloc)
     }
   }
   if (fresh) {
-    // the chain kernel's counters start at zero; every launch leaves them at zero
-    if (cudaMemset(c->chain_bar, 0, bar_b) != cudaSuccess) {
+    // the chain kernel's counters start at zero (every launch leaves them at
+    // zero; its launch counter only grows) and so do its tag words (tag 0
+    // is never a launch's)
+    if (cudaMemset(c->chain_bar, 0, bar_b + tag_b) != cudaSuccess) {
       cudaGetLastError();
       set_error("workspace initialisation failed");
       return ST_DEVICE;
@@ -610,6 +631,9 @@ static int enqueue(const Model* m, const Replica* rep, ExecCtx* c, const float* 
     p.bar = c->chain_bar;
     p.err = rep->err_dev;
     p.stall_test = m->tc_stall_test.load();
+    // tagged hand-over: the layers whose outputs a later layer reads
+    size_t tag_next = 0;
+    bool tags_ok = c->chain_tags != nullptr;
     for (size_t i = 0; i < rep->steps.size() && take; ++i) {
       const Step& st = rep->steps[i];
       const TuneRecord* tr = st.tuned_for(batch);
@@ -624,7 +648,22 @@ static int enqueue(const Model* m, const Replica* rep, ExecCtx* c, const float* 
       L.N = (int)st.N;
       L.epi = st.epi;
       if (reinterpret_cast<uintptr_t>(L.a) & 15u) take = false;  // float4 rows
+      L.tag_off = -1;
+      L.a_src = -1;
+      L.res_src = -1;
+      for (size_t j = 0; j < i; ++j) {
+        const float* out_j = ptr(rep->steps[j].out);
+        if (out_j == L.a) L.a_src = (int)j;
+        if (L.res && out_j == L.res) L.res_src = (int)j;
+      }
+      for (int src : {L.a_src, L.res_src}) {
+        if (src >= 0 && p.layer[src].tag_off < 0) {
+          p.layer[src].tag_off = (int)tag_next;
+          tag_next += (size_t)batch * (size_t)rep->steps[(size_t)src].N;
+        }
+      }
     }
+    if (tags_ok && batch <= kChainTagRows && tag_next <= c->chain_tag_words) p.tags = c->chain_tags;
     const size_t smem = take ? chain_plan(p, rep->chain_grid) : 0;
     if (take && smem > 0) {
       if (marks) cudaEventRecord(marks[0], s);
@@ -921,7 +960,7 @@ static int enqueue(const Model* m, const Replica* rep, ExecCtx* c, const float* 
 static int check_kernel_error(const Replica* rep) {
   const volatile int* e = rep->err_host;
   if (e && *e != 0) {
-    set_error("kernel aborted: a bounded wait (tensor-core pipeline or grid barrier) exceeded its limit (code " +
+    set_error("kernel aborted: a bounded wait (tensor-core pipeline, grid barrier or hand-over) exceeded its limit (code " +
               std::to_string(*e) + ")");
     return ST_DEVICE;
   }

@@ -9,8 +9,10 @@ L2 otherwise.
 * results are bitwise identical run to run;
 * launch lists it cannot run (K not a multiple of 4, an elementwise node,
   an input pointer that is not 16-byte aligned) keep the per-layer kernels;
-* a grid-barrier wait that runs out is reported as -5 and the context then
-  computes correctly again (no GPU fault).
+* a wait for another CTA's values that runs out (up to 8 rows each value a
+  tagged word and the layers hand over without grid barriers; at 16 rows a
+  grid barrier) is reported as -5 and the context then computes correctly
+  again (no GPU fault).
 """
 
 import numpy as np
@@ -118,15 +120,19 @@ def test_chain_declines_what_it_cannot_run(tmp_path):
     cm2.close()
 
 
-def test_chain_barrier_timeout_is_reported_and_recoverable(tmp_path):
-    """The failure-detection hook makes CTA 0 leave without arriving at the
-    first grid barrier: the other CTAs' bounded waits run out (about 2 s),
-    they record the error and leave, the last one out resets the counters;
-    the run returns -5 and the next run is correct."""
+@pytest.mark.parametrize("rows", [4, 16])
+def test_chain_barrier_timeout_is_reported_and_recoverable(rows, tmp_path):
+    """The failure-detection hook makes CTA 0 leave without computing: the
+    other CTAs' bounded waits run out (about 2 s) -- at 4 rows for its
+    layer-1 values (tagged words), at 16 rows at the first grid barrier --
+    they record the error and leave, the last one out resets the counters
+    and advances the launch counter, so the next launch's tag differs from
+    any word written before; the run returns -5 and the next run is
+    correct."""
     m = workloads.tiny_mlp()
     cm, eng = engine(m, (784,), tmp_path)
-    x = workloads.seeded_input((4, 784)).numpy()
-    y = np.zeros((4, 10), np.float32)
+    x = workloads.seeded_input((rows, 784)).numpy()
+    y = np.zeros((rows, 10), np.float32)
     want = oracle.run_model(m, x, "fused_ikj")
     assert eng.run(x, y) == 0
     assert np.allclose(y, want, atol=ATOL, rtol=RTOL)
