@@ -81,6 +81,7 @@ struct ChainParams {
   int M;
   unsigned long long* bar;  // [0] arrivals, [1] departures (zero between launches), [3] launch counter
   unsigned long long* tags; // tag area (tagged hand-over), or null (grid barriers)
+  unsigned* done;           // mapped host word the last CTA out sets to 1 (output visible), or null
   int* err;                 // the replica's error word (mapped host memory)
   int stall_test;           // failure-detection hook: CTA 0 never arrives at the first barrier
   int xs_floats;            // shared memory for the input rows (floats, a multiple of 4)
@@ -358,12 +359,19 @@ __global__ void __launch_bounds__(kChainWarps * 32, 1) chain_gemv_kernel(const _
   // departure: the last CTA out resets both counters for the next launch
   __syncthreads();
   if (threadIdx.x == 0) {
-    __threadfence();
+    // with a completion word, this CTA's output (in mapped host memory) is
+    // made visible to the host before it counts itself out
+    if (p.done) __threadfence_system();
+    else __threadfence();
     const unsigned long long d = atomicAdd(p.bar + 1, 1ull);
     if (d == gridDim.x - 1) {
       atomicExch(p.bar, 0ull);
       atomicExch(p.bar + 1, 0ull);
       if (tagged) atomicExch(p.bar + 3, epoch);  // the next launch tags with epoch + 1
+      if (p.done) {
+        __threadfence_system();
+        *reinterpret_cast<volatile unsigned*>(p.done) = 1u;
+      }
     }
   }
 }

@@ -133,6 +133,10 @@ struct ExecCtx {
   float* h_out = nullptr;
   float* h_in_dev = nullptr;  // device addresses of the mapped staging buffers
   float* h_out_dev = nullptr;
+  // completion word of a small chain run (mapped): the kernel's last CTA
+  // sets it after its output is visible to the host
+  volatile unsigned* h_done = nullptr;
+  unsigned* h_done_dev = nullptr;
   struct CachedGraph {
     int64_t batch;
     const float* in;
@@ -191,6 +195,7 @@ static void destroy_ctx(ExecCtx* c) {
   if (c->block) cudaFree(c->block);
   if (c->h_in) cudaFreeHost(c->h_in);
   if (c->h_out) cudaFreeHost(c->h_out);
+  if (c->h_done) cudaFreeHost(const_cast<unsigned*>(c->h_done));
   delete c;
 }
 
@@ -630,6 +635,7 @@ static int enqueue(const Model* m, const Replica* rep, ExecCtx* c, const float* 
     p.M = (int)batch;
     p.bar = c->chain_bar;
     p.err = rep->err_dev;
+    p.done = (in == c->h_in_dev && c->h_done_dev) ? c->h_done_dev : nullptr;
     p.stall_test = m->tc_stall_test.load();
     // tagged hand-over: the layers whose outputs a later layer reads
     size_t tag_next = 0;
@@ -1092,9 +1098,24 @@ static int run_host_one(Model* m, int dev, const float* in, float* out, int64_t 
           set_error("pinned host staging allocation failed");
           return ST_ALLOC;
         }
+        unsigned* done = nullptr;
+        if (cudaHostAlloc(reinterpret_cast<void**>(&done), 64, cudaHostAllocMapped) != cudaSuccess ||
+            cudaHostGetDevicePointer(reinterpret_cast<void**>(&c->h_done_dev), done, 0) != cudaSuccess) {
+          cudaGetLastError();
+          if (done) cudaFreeHost(done);
+          c->h_done_dev = nullptr;  // completion by stream query only
+        } else {
+          c->h_done = done;
+        }
       }
       std::memcpy(c->h_in, in, in_b);
-      if (chain_takes(m, rep, batch) && in_b * (size_t)rep->chain_grid <= kZeroCopyReadBytes) {
+      const bool zero_copy = chain_takes(m, rep, batch) && in_b * (size_t)rep->chain_grid <= kZeroCopyReadBytes;
+      const bool by_word = zero_copy && c->h_done;
+      if (by_word) {
+        *c->h_done = 0u;  // the previous run's word was seen: no write of it is in flight
+        std::atomic_thread_fence(std::memory_order_seq_cst);
+      }
+      if (zero_copy) {
         // the one-launch chain reads its input rows from and writes its
         // output to the mapped staging buffers itself: no copy at all
         rc = run_graph(m, rep, c, c->h_in_dev, c->h_out_dev, batch, c->stream);
@@ -1102,11 +1123,20 @@ static int run_host_one(Model* m, int dev, const float* in, float* out, int64_t 
         rc = run_graph(m, rep, c, c->d_in, c->d_out, batch, c->stream, true, in_b, out_b);
       }
       if (rc) return rc;
-      // a few microseconds of work: poll instead of sleeping in the driver
-      cudaError_t q;
-      while ((q = cudaStreamQuery(c->stream)) == cudaErrorNotReady) {
+      // a few microseconds of work: poll instead of sleeping in the driver --
+      // the chain kernel's completion word where it has one (the output is
+      // visible to the host once it is set), with the stream queried now and
+      // then for errors; else the stream
+      cudaError_t q = cudaSuccess;
+      for (uint64_t it = 0;; ++it) {
+        if (by_word && *c->h_done) break;
+        if (!by_word || (it & 255u) == 255u) {
+          q = cudaStreamQuery(c->stream);
+          if (q != cudaErrorNotReady) break;
+        }
       }
-      if (q != cudaSuccess) {
+      std::atomic_thread_fence(std::memory_order_acquire);
+      if (q != cudaSuccess && q != cudaErrorNotReady) {
         set_error(std::string("small run: ") + cudaGetErrorString(q));
         return ST_DEVICE;
       }
